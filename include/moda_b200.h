@@ -1,0 +1,104 @@
+/*
+ * moda_b200.h - C ABI of the B200 (sm_100a) fused MoDA forward library.
+ *
+ * Plain pointers and sizes only: no PyTorch types cross this boundary. The
+ * caller owns every buffer; the library never allocates device memory on the
+ * compute path. Kernels launch on the caller's stream; no call synchronizes
+ * the host.
+ *
+ * Each entry point names the reference interface it replaces
+ * (sahilmalik27/mixture-of-depth-attention, paths relative to that project).
+ */
+#ifndef MODA_B200_H_
+#define MODA_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* A rank-4 strided view. sizes/strides are in elements, outermost first,
+ * exactly torch.Tensor.size()/.stride() of a [B, H, rows, d] tensor. */
+typedef struct ModaTensor {
+    void* ptr;
+    int64_t sizes[4];
+    int64_t strides[4];
+} ModaTensor;
+
+typedef void* moda_stream_t; /* a cudaStream_t (torch.cuda.current_stream().cuda_stream) */
+
+enum ModaDtype { MODA_F32 = 0, MODA_BF16 = 1, MODA_F16 = 2 };
+
+enum ModaStatus {
+    MODA_OK = 0,
+    MODA_ERR_ARG = -1,        /* null pointer, bad num_layers / scale / layer index */
+    MODA_ERR_SHAPE = -2,      /* inconsistent B, H, T or d between tensors */
+    MODA_ERR_DEPTH_ROWS = -3, /* depth buffer holds fewer than T*num_layers rows */
+    MODA_ERR_DTYPE = -4,      /* unknown dtype code */
+    MODA_ERR_LAUNCH = -5,     /* CUDA reported an error at launch */
+    MODA_ERR_UNSUPPORTED = -6 /* a forced kernel cannot run this shape/layout */
+};
+
+/* Kernel selection for moda_fwd_ex (moda_fwd uses MODA_KERNEL_AUTO). */
+enum ModaKernel {
+    MODA_KERNEL_AUTO = 0, /* tcgen05 path when the shape allows it, else SIMT */
+    MODA_KERNEL_TC = 1,   /* TMA + tcgen05/TMEM fused kernel (bf16/f16, d in {64,128}) */
+    MODA_KERNEL_SIMT = 2  /* CUDA-core kernel: any dtype, any strides, d <= 256 */
+};
+
+/*
+ * Fused sequence + depth attention forward:
+ *   O[b,h,t] = softmax over { scale*q.k_j : j <= t }  U  { scale*q.kd_{t*L+l} : l < L }
+ *              applied to the matching V / V_depth rows, with KV head h / (H_q/H_k).
+ * q [B,H_q,T,d]; k, v [B,H_k,T,d]; kd, vd [B,H_k,R,d] with R >= T*num_layers
+ * (only rows [0, T*num_layers) are read); o [B,H_q,T,d] written in full.
+ * scale <= 0 selects d^-0.5. chunk_size is accepted for signature parity and
+ * does not change the result (the function is chunk-invariant); pass 0 for none.
+ *
+ * Replaces moda_attention_triton (moda/kernels/moda_triton.py:218-297) and
+ * moda_attention_naive (moda/kernels/moda_naive.py:13-97), reached from
+ * MoDAAttention.forward (moda/attention.py:85-93).
+ */
+int moda_fwd(const ModaTensor* q, const ModaTensor* k, const ModaTensor* v, const ModaTensor* kd,
+             const ModaTensor* vd, const ModaTensor* o, int num_layers, float scale,
+             int chunk_size, int dtype, moda_stream_t stream);
+
+/* moda_fwd with an explicit kernel choice (ModaKernel). Same reference counterpart. */
+int moda_fwd_ex(const ModaTensor* q, const ModaTensor* k, const ModaTensor* v,
+                const ModaTensor* kd, const ModaTensor* vd, const ModaTensor* o, int num_layers,
+                float scale, int chunk_size, int dtype, int kernel, moda_stream_t stream);
+
+/* Which kernel moda_fwd_ex would launch for these arguments (ModaKernel value,
+ * or a negative ModaStatus). Host-only: validates and plans, launches nothing.
+ * No reference counterpart (the reference picks its path in Python,
+ * moda/attention.py:48,87). */
+int moda_fwd_plan(const ModaTensor* q, const ModaTensor* k, const ModaTensor* v,
+                  const ModaTensor* kd, const ModaTensor* vd, const ModaTensor* o, int num_layers,
+                  int dtype, int kernel);
+
+/*
+ * Depth-cache append: k_cache[b,h,t*L + layer_idx,:] = k_src[b,h,t,:] for t < seq_len,
+ * and the same for v, in one launch. k_src/v_src [B,H_k,>=seq_len,d];
+ * caches [B,H_k,>=seq_len*L,d]; any strides.
+ * Replaces DepthKVCache.write (moda/cache.py:52-74).
+ */
+int moda_depth_append(const ModaTensor* k_src, const ModaTensor* v_src, const ModaTensor* k_cache,
+                      const ModaTensor* v_cache, int layer_idx, int num_layers, int seq_len,
+                      int dtype, moda_stream_t stream);
+
+/* Text of the last error on the calling thread ("" if none). Thread-local. */
+const char* moda_last_error(void);
+
+/* Reads and clears the device status word kernels set when a bounded wait
+ * times out (0 = none). Synchronizes `stream`. No reference counterpart. */
+int moda_device_status(moda_stream_t stream);
+
+/* Library version (major*10000 + minor*100 + patch). */
+int moda_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MODA_B200_H_ */

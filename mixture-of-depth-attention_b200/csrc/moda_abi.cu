@@ -1,0 +1,231 @@
+// C ABI of the MoDA B200 library: argument validation, kernel planning, launch.
+//
+// All checks run on the host before any launch; a rejected call returns a
+// negative ModaStatus and leaves its text in a thread-local buffer
+// (moda_last_error). Nothing here allocates device memory.
+#include "moda_internal.h"
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof(g_err), fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+bool dtype_ok(int dtype) { return dtype == MODA_F32 || dtype == MODA_BF16 || dtype == MODA_F16; }
+
+// Validation mirrors what moda_attention_naive (moda/kernels/moda_naive.py:44-59)
+// needs to produce a result, plus the explicit depth-row check that the
+// reference leaves to a late shape error (moda_naive.py:137-149).
+int validate_fwd(const ModaTensor* q, const ModaTensor* k, const ModaTensor* v,
+                 const ModaTensor* kd, const ModaTensor* vd, const ModaTensor* o, int num_layers,
+                 float scale, int dtype, moda::FwdParams* out) {
+    if (!q || !k || !v || !kd || !vd || !o) return fail(MODA_ERR_ARG, "null tensor descriptor");
+    if (!dtype_ok(dtype)) return fail(MODA_ERR_DTYPE, "unknown dtype code %d", dtype);
+    const ModaTensor* all[6] = {q, k, v, kd, vd, o};
+    const char* names[6] = {"Q", "K", "V", "K_depth", "V_depth", "O"};
+    for (int i = 0; i < 6; ++i) {
+        for (int j = 0; j < 4; ++j)
+            if (all[i]->sizes[j] < 0) return fail(MODA_ERR_SHAPE, "%s has a negative size", names[i]);
+    }
+    const int64_t B = q->sizes[0], Hq = q->sizes[1], T = q->sizes[2], d = q->sizes[3];
+    const int64_t Hk = k->sizes[1];
+    if (num_layers < 0) return fail(MODA_ERR_ARG, "num_layers must be >= 0, got %d", num_layers);
+    if (Hk <= 0 || Hq % Hk != 0)
+        return fail(MODA_ERR_SHAPE, "H_q (%lld) must be a multiple of H_k (%lld)", (long long)Hq,
+                    (long long)Hk);
+    if (d <= 0 || d > 256) return fail(MODA_ERR_SHAPE, "head_dim must be in [1, 256], got %lld", (long long)d);
+    auto same = [&](const ModaTensor* t, const char* n, int64_t b, int64_t h, int64_t rows_min,
+                    bool exact_rows) -> int {
+        if (t->sizes[0] != b || t->sizes[1] != h || t->sizes[3] != d)
+            return fail(MODA_ERR_SHAPE, "%s has shape [%lld,%lld,%lld,%lld], expected [%lld,%lld,*,%lld]",
+                        n, (long long)t->sizes[0], (long long)t->sizes[1], (long long)t->sizes[2],
+                        (long long)t->sizes[3], (long long)b, (long long)h, (long long)d);
+        if (exact_rows ? t->sizes[2] != rows_min : t->sizes[2] < rows_min)
+            return fail(MODA_ERR_SHAPE, "%s has %lld rows, expected %s%lld", n,
+                        (long long)t->sizes[2], exact_rows ? "" : ">= ", (long long)rows_min);
+        return MODA_OK;
+    };
+    int r;
+    if ((r = same(k, "K", B, Hk, T, true)) || (r = same(v, "V", B, Hk, T, true)) ||
+        (r = same(o, "O", B, Hq, T, true)))
+        return r;
+    const int64_t need = T * static_cast<int64_t>(num_layers);
+    for (int i = 3; i < 5; ++i) {
+        const ModaTensor* t = all[i];
+        if (t->sizes[0] != B || t->sizes[1] != Hk || t->sizes[3] != d)
+            return fail(MODA_ERR_SHAPE, "%s has shape [%lld,%lld,%lld,%lld], expected [%lld,%lld,>=T*L,%lld]",
+                        names[i], (long long)t->sizes[0], (long long)t->sizes[1],
+                        (long long)t->sizes[2], (long long)t->sizes[3], (long long)B,
+                        (long long)Hk, (long long)d);
+        if (t->sizes[2] < need)
+            return fail(MODA_ERR_DEPTH_ROWS,
+                        "%s holds %lld rows but T*num_layers = %lld*%d = %lld rows are addressed",
+                        names[i], (long long)t->sizes[2], (long long)T, num_layers, (long long)need);
+    }
+    const int64_t numel = B * Hq * T * d;
+    for (int i = 0; i < 6; ++i) {
+        int64_t n = 1;
+        for (int j = 0; j < 4; ++j) n *= all[i]->sizes[j];
+        if (n > 0 && !all[i]->ptr) return fail(MODA_ERR_ARG, "%s has a null data pointer", names[i]);
+    }
+    if (B > 65535 || Hq > 65535)
+        return fail(MODA_ERR_SHAPE, "batch and head counts must be <= 65535");
+    if (T > 0x7fffffff || need > 0x7fffffffLL)
+        return fail(MODA_ERR_SHAPE, "T and T*num_layers must fit in 31 bits");
+    (void)numel;
+    out->q = *q;
+    out->k = *k;
+    out->v = *v;
+    out->kd = *kd;
+    out->vd = *vd;
+    out->o = *o;
+    out->B = static_cast<int>(B);
+    out->Hq = static_cast<int>(Hq);
+    out->Hk = static_cast<int>(Hk);
+    out->G = static_cast<int>(Hq / Hk);
+    out->T = static_cast<int>(T);
+    out->d = static_cast<int>(d);
+    out->L = num_layers;
+    out->scale = scale > 0.f ? scale : 1.0f / sqrtf(static_cast<float>(d));
+    out->dtype = dtype;
+    return MODA_OK;
+}
+
+int plan_kernel(const moda::FwdParams& p, int kernel) {
+    char why[256];
+    switch (kernel) {
+        case MODA_KERNEL_SIMT: return MODA_KERNEL_SIMT;
+        case MODA_KERNEL_TC:
+            if (!moda::tc_supports(p, why, sizeof(why)))
+                return fail(MODA_ERR_UNSUPPORTED, "tcgen05 kernel forced but %s", why);
+            return MODA_KERNEL_TC;
+        case MODA_KERNEL_AUTO:
+            return moda::tc_supports(p, why, sizeof(why)) ? MODA_KERNEL_TC : MODA_KERNEL_SIMT;
+        default: return fail(MODA_ERR_ARG, "unknown kernel selector %d", kernel);
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+int moda_fwd_plan(const ModaTensor* q, const ModaTensor* k, const ModaTensor* v,
+                  const ModaTensor* kd, const ModaTensor* vd, const ModaTensor* o, int num_layers,
+                  int dtype, int kernel) {
+    g_err[0] = 0;
+    moda::FwdParams p;
+    int r = validate_fwd(q, k, v, kd, vd, o, num_layers, 0.f, dtype, &p);
+    if (r != MODA_OK) return r;
+    return plan_kernel(p, kernel);
+}
+
+int moda_fwd_ex(const ModaTensor* q, const ModaTensor* k, const ModaTensor* v,
+                const ModaTensor* kd, const ModaTensor* vd, const ModaTensor* o, int num_layers,
+                float scale, int chunk_size, int dtype, int kernel, moda_stream_t stream) {
+    g_err[0] = 0;
+    if (chunk_size < 0) return fail(MODA_ERR_ARG, "chunk_size must be >= 0 (0 = none), got %d", chunk_size);
+    moda::FwdParams p;
+    int r = validate_fwd(q, k, v, kd, vd, o, num_layers, scale, dtype, &p);
+    if (r != MODA_OK) return r;
+    const int which = plan_kernel(p, kernel);
+    if (which < 0) return which;
+    if (static_cast<int64_t>(p.B) * p.Hq * p.T * p.d == 0) return MODA_OK;  // nothing to write
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cudaGetLastError();  // clear a stale error so the check below is ours
+    if (which == MODA_KERNEL_TC) {
+        char err[256] = "";
+        r = moda::launch_fwd_tc(p, st, err, sizeof(err));
+        if (r != MODA_OK) return fail(r, "%s", err[0] ? err : "tcgen05 launch failed");
+    } else {
+        r = moda::launch_fwd_simt(p, st);
+        if (r != MODA_OK) return fail(r, "SIMT launch rejected");
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(MODA_ERR_LAUNCH, "CUDA launch error: %s", cudaGetErrorString(e));
+    return MODA_OK;
+}
+
+int moda_fwd(const ModaTensor* q, const ModaTensor* k, const ModaTensor* v, const ModaTensor* kd,
+             const ModaTensor* vd, const ModaTensor* o, int num_layers, float scale,
+             int chunk_size, int dtype, moda_stream_t stream) {
+    return moda_fwd_ex(q, k, v, kd, vd, o, num_layers, scale, chunk_size, dtype, MODA_KERNEL_AUTO,
+                       stream);
+}
+
+int moda_depth_append(const ModaTensor* k_src, const ModaTensor* v_src, const ModaTensor* k_cache,
+                      const ModaTensor* v_cache, int layer_idx, int num_layers, int seq_len,
+                      int dtype, moda_stream_t stream) {
+    g_err[0] = 0;
+    if (!k_src || !v_src || !k_cache || !v_cache) return fail(MODA_ERR_ARG, "null tensor descriptor");
+    if (!dtype_ok(dtype)) return fail(MODA_ERR_DTYPE, "unknown dtype code %d", dtype);
+    if (num_layers <= 0) return fail(MODA_ERR_ARG, "num_layers must be > 0, got %d", num_layers);
+    if (layer_idx < 0 || layer_idx >= num_layers)
+        return fail(MODA_ERR_ARG, "layer_idx %d outside [0, %d)", layer_idx, num_layers);
+    if (seq_len < 0) return fail(MODA_ERR_ARG, "seq_len must be >= 0");
+    const int64_t B = k_cache->sizes[0], H = k_cache->sizes[1], d = k_cache->sizes[3];
+    const ModaTensor* src[2] = {k_src, v_src};
+    const ModaTensor* dst[2] = {k_cache, v_cache};
+    for (int i = 0; i < 2; ++i) {
+        if (src[i]->sizes[0] != B || src[i]->sizes[1] != H || src[i]->sizes[3] != d ||
+            dst[i]->sizes[0] != B || dst[i]->sizes[1] != H || dst[i]->sizes[3] != d)
+            return fail(MODA_ERR_SHAPE, "depth append: batch/head/head_dim mismatch");
+        if (src[i]->sizes[2] < seq_len)
+            return fail(MODA_ERR_SHAPE, "depth append: source has %lld rows < seq_len %d",
+                        (long long)src[i]->sizes[2], seq_len);
+        if (dst[i]->sizes[2] < static_cast<int64_t>(seq_len) * num_layers)
+            return fail(MODA_ERR_DEPTH_ROWS, "depth append: cache has %lld rows < seq_len*L = %lld",
+                        (long long)dst[i]->sizes[2], (long long)seq_len * num_layers);
+    }
+    if (B * H * seq_len * d == 0) return MODA_OK;
+    moda::AppendParams p;
+    p.k_src = *k_src;
+    p.v_src = *v_src;
+    p.k_cache = *k_cache;
+    p.v_cache = *v_cache;
+    p.B = static_cast<int>(B);
+    p.H = static_cast<int>(H);
+    p.T = seq_len;
+    p.d = static_cast<int>(d);
+    p.L = num_layers;
+    p.layer = layer_idx;
+    p.dtype = dtype;
+    const int esz = dtype == MODA_F32 ? 4 : 2;
+    bool vec16 = (d * esz) % 16 == 0;
+    for (int i = 0; i < 2 && vec16; ++i) {
+        const ModaTensor* ts[2] = {src[i], dst[i]};
+        for (const ModaTensor* t : ts) {
+            if (t->strides[3] != 1 || reinterpret_cast<uintptr_t>(t->ptr) % 16 != 0) vec16 = false;
+            for (int j = 0; j < 3; ++j)
+                if ((t->strides[j] * esz) % 16 != 0) vec16 = false;
+        }
+    }
+    cudaGetLastError();
+    int r = moda::launch_depth_append(p, vec16, static_cast<cudaStream_t>(stream));
+    if (r != MODA_OK) return fail(r, "depth append launch rejected");
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(MODA_ERR_LAUNCH, "CUDA launch error: %s", cudaGetErrorString(e));
+    return MODA_OK;
+}
+
+const char* moda_last_error(void) { return g_err; }
+
+int moda_device_status(moda_stream_t stream) {
+    int v = 0;
+    if (moda::read_and_clear_status(static_cast<cudaStream_t>(stream), &v) != cudaSuccess)
+        return fail(MODA_ERR_LAUNCH, "could not read the device status word");
+    return v;
+}
+
+int moda_version(void) { return 100; }
+
+}  // extern "C"

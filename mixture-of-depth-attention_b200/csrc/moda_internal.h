@@ -1,0 +1,38 @@
+// Internal declarations shared by the MoDA CUDA sources (not part of the C ABI).
+#pragma once
+
+#include "../../include/moda_b200.h"
+#include "moda_common.cuh"
+
+namespace moda {
+
+// Validated forward problem. Strides are in elements.
+struct FwdParams {
+    ModaTensor q, k, v, kd, vd, o;
+    int B, Hq, Hk, G, T, d, L;
+    float scale;
+    int dtype;
+};
+
+struct AppendParams {
+    ModaTensor k_src, v_src, k_cache, v_cache;
+    int B, H, T, d, L, layer;
+    int dtype;
+};
+
+// Parameters of the tcgen05 kernel. Tensor maps first (64-byte aligned).
+struct TcParams {
+    CUtensorMap tm_q, tm_k, tm_v, tm_kd, tm_vd, tm_o;
+    int B, Hq, Hk, G, T, L;
+    int n_tok;      // tokens per 128-row query tile (128 / G)
+    int num_pairs;  // tile pairs per (b, kv head)
+    float sc;       // scale * log2(e)
+};
+
+int launch_fwd_simt(const FwdParams& p, cudaStream_t stream);
+int launch_fwd_tc(const FwdParams& p, cudaStream_t stream, char* err, size_t errlen);
+bool tc_supports(const FwdParams& p, char* why, size_t whylen);
+int launch_depth_append(const AppendParams& p, bool vec16, cudaStream_t stream);
+cudaError_t read_and_clear_status(cudaStream_t stream, int* value);
+
+}  // namespace moda

@@ -1,0 +1,77 @@
+"""MoDAAttention with the B200 fused kernel (reference: moda/attention.py:16-116).
+
+Same parameters (q_proj, k_proj, v_proj, o_proj, k_depth_proj, v_depth_proj),
+same forward signature and outputs. Every attention call -- with depth
+(attention.py:85-93) or without (attention.py:94-96, 104-116) -- runs
+``moda_attention_cuda``; without depth it is the same kernel with L = 0, i.e.
+plain causal attention with in-kernel GQA.
+"""
+
+from typing import Optional
+
+import torch
+import torch.nn as nn
+from torch import Tensor
+
+from .config import MoDAConfig
+from .kernels.moda_cuda import moda_attention_cuda
+
+
+class MoDAAttention(nn.Module):
+    """Mixture-of-Depths Attention.
+
+    Attends to the causal sequence KV of this layer and to the depth KV that
+    preceding layers wrote for the same token, in one softmax.
+    """
+
+    def __init__(self, config: MoDAConfig):
+        super().__init__()
+        self.config = config
+        self.num_heads = config.num_heads
+        self.num_kv_heads = config.num_kv_heads
+        self.head_dim = config.head_dim
+        self.num_layers = config.num_layers
+        self.scale = config.head_dim ** -0.5
+        self.q_proj = nn.Linear(config.d_model, config.num_heads * config.head_dim, bias=False)
+        self.k_proj = nn.Linear(config.d_model, config.num_kv_heads * config.head_dim, bias=False)
+        self.v_proj = nn.Linear(config.d_model, config.num_kv_heads * config.head_dim, bias=False)
+        self.o_proj = nn.Linear(config.num_heads * config.head_dim, config.d_model, bias=False)
+        self.k_depth_proj = nn.Linear(config.d_model, config.num_kv_heads * config.head_dim,
+                                      bias=False)
+        self.v_depth_proj = nn.Linear(config.d_model, config.num_kv_heads * config.head_dim,
+                                      bias=False)
+        self.use_triton = False  # kept for API parity; there is one CUDA path
+        self.dropout = nn.Dropout(config.dropout) if config.dropout > 0 else nn.Identity()
+
+    def forward(self, x: Tensor, K_depth: Optional[Tensor] = None,
+                V_depth: Optional[Tensor] = None) -> tuple[Tensor, Tensor, Tensor]:
+        """Forward pass.
+
+        Args:
+            x: [B, T, D] input (CUDA).
+            K_depth: [B, H_k, T*L', d] depth keys from preceding layers, or None.
+            V_depth: [B, H_k, T*L', d] depth values, or None.
+
+        Returns:
+            (output [B, T, D], k_write [B, H_k, T, d], v_write [B, H_k, T, d]).
+        """
+        B, T, D = x.shape
+        H_q, H_k, d = self.num_heads, self.num_kv_heads, self.head_dim
+        # [B, H, T, d] views with strides (T*H*d, d, H*d, 1): the kernel reads them in place
+        Q = self.q_proj(x).view(B, T, H_q, d).transpose(1, 2)
+        K = self.k_proj(x).view(B, T, H_k, d).transpose(1, 2)
+        V = self.v_proj(x).view(B, T, H_k, d).transpose(1, 2)
+        k_write = self.k_depth_proj(x).view(B, T, H_k, d).transpose(1, 2)
+        v_write = self.v_depth_proj(x).view(B, T, H_k, d).transpose(1, 2)
+
+        if K_depth is not None and V_depth is not None and K_depth.shape[2] > 0:
+            out = moda_attention_cuda(Q, K, V, K_depth, V_depth, num_layers=self.num_layers,
+                                      scale=self.scale, chunk_size=self.config.chunk_size)
+        else:
+            empty = Q.new_empty(B, H_k, 0, d)
+            out = moda_attention_cuda(Q, K, V, empty, empty, num_layers=0, scale=self.scale)
+
+        out = out.transpose(1, 2).contiguous().view(B, T, H_q * d)
+        out = self.o_proj(out)
+        out = self.dropout(out)
+        return out, k_write, v_write

@@ -1,0 +1,67 @@
+"""Depth KV cache with the reference layout (moda/cache.py:8-95).
+
+Token t's depth entries occupy rows [t*L, (t+1)*L) of
+k_cache/v_cache [B, H_k, max_seq_len*L, d]; row t*L + l holds layer l. The
+write is one fused CUDA launch for k and v (``moda_depth_append``) instead of
+two strided slice copies (cache.py:73-74).
+"""
+
+from typing import Optional
+
+import torch
+from torch import Tensor
+
+from .kernels.moda_cuda import depth_append
+
+
+class DepthKVCache:
+    """Depth KV cache shared by all layers of one forward pass.
+
+    Same constructor, ``write``, ``read`` and ``reset`` as the reference. The
+    buffers are zero-initialised like the reference's (cache.py:38-47), so
+    unwritten slots read as zeros.
+    """
+
+    def __init__(self, batch_size: int, max_seq_len: int, num_layers: int, num_kv_heads: int,
+                 head_dim: int, device: Optional[torch.device] = None,
+                 dtype: Optional[torch.dtype] = None):
+        self.batch_size = batch_size
+        self.max_seq_len = max_seq_len
+        self.num_layers = num_layers
+        self.num_kv_heads = num_kv_heads
+        self.head_dim = head_dim
+        total_depth = max_seq_len * num_layers
+        self.k_cache = torch.zeros(batch_size, num_kv_heads, total_depth, head_dim,
+                                   device=device, dtype=dtype)
+        self.v_cache = torch.zeros(batch_size, num_kv_heads, total_depth, head_dim,
+                                   device=device, dtype=dtype)
+        self._layer_count = 0
+        self._seq_len = 0
+
+    def write(self, layer_idx: int, k_depth: Tensor, v_depth: Tensor,
+              seq_len: Optional[int] = None):
+        """Write layer ``layer_idx``'s depth KV: row t*L + layer_idx <- token t.
+
+        Args:
+            layer_idx: Which layer is writing (0 to num_layers-1).
+            k_depth: [B, H_k, T, d] depth keys (any strides).
+            v_depth: [B, H_k, T, d] depth values.
+            seq_len: Sequence length (defaults to k_depth.shape[2]).
+        """
+        T = seq_len or k_depth.shape[2]
+        self._seq_len = max(self._seq_len, T)
+        depth_append(self.k_cache, self.v_cache, layer_idx, k_depth, v_depth,
+                     self.num_layers, T)
+
+    def read(self, seq_len: Optional[int] = None) -> tuple[Tensor, Tensor]:
+        """Views [B, H_k, T*L, d] of the first T tokens' depth rows (cache.py:76-88)."""
+        T = seq_len or self._seq_len
+        total = T * self.num_layers
+        return self.k_cache[:, :, :total], self.v_cache[:, :, :total]
+
+    def reset(self):
+        """Clear the cache."""
+        self.k_cache.zero_()
+        self.v_cache.zero_()
+        self._layer_count = 0
+        self._seq_len = 0

@@ -1,0 +1,189 @@
+"""B200 CUDA MoDA attention behind the reference kernel signature.
+
+``moda_attention_cuda(Q, K, V, K_depth, V_depth, num_layers, scale=None,
+chunk_size=None)`` keeps the positional/keyword order of
+``moda_attention_naive`` (moda/kernels/moda_naive.py:13-22) and
+``moda_attention_triton`` (moda/kernels/moda_triton.py:218-227) and computes the
+same function: one softmax over the causal sequence keys and the token's own L
+depth rows. The forward always runs in libmoda_b200.so (tcgen05 kernel for
+bf16/f16 with d in {64,128}, CUDA-core kernel otherwise); CPU tensors raise.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+from torch import Tensor
+
+from . import _lib
+
+_DTYPES = {torch.float32: _lib.MODA_F32, torch.bfloat16: _lib.MODA_BF16,
+           torch.float16: _lib.MODA_F16}
+_KERNELS = {"auto": _lib.KERNEL_AUTO, "tc": _lib.KERNEL_TC, "simt": _lib.KERNEL_SIMT}
+
+
+def _desc(t: Tensor) -> _lib.ModaTensor:
+    return _lib.describe(t.data_ptr(), t.shape, t.stride())
+
+
+def _check_inputs(Q, K, V, K_depth, V_depth):
+    ts = (Q, K, V, K_depth, V_depth)
+    names = ("Q", "K", "V", "K_depth", "V_depth")
+    for n, t in zip(names, ts):
+        if not isinstance(t, Tensor):
+            raise TypeError(f"{n} must be a torch.Tensor")
+        if t.dim() != 4:
+            raise _lib.MoDAShapeError(f"{n} must be 4-D [B, H, rows, d], got shape {tuple(t.shape)}")
+        if t.device.type != "cuda":
+            raise RuntimeError(
+                f"moda_attention_cuda runs on CUDA tensors only ({n} is on {t.device}); "
+                "there is no CPU path")
+        if t.dtype not in _DTYPES:
+            raise TypeError(f"{n} has unsupported dtype {t.dtype} (float32, bfloat16, float16)")
+    dev, dt = Q.device, Q.dtype
+    for n, t in zip(names, ts):
+        if t.device != dev:
+            raise RuntimeError(f"{n} is on {t.device}, Q on {dev}")
+        if t.dtype != dt:
+            raise TypeError(f"{n} has dtype {t.dtype}, Q has {dt}")
+
+
+def moda_forward_into(O: Tensor, Q: Tensor, K: Tensor, V: Tensor, K_depth: Tensor,
+                      V_depth: Tensor, num_layers: int, scale: Optional[float] = None,
+                      chunk_size: Optional[int] = None, kernel: str = "auto") -> Tensor:
+    """Run the forward into a preallocated O [B,H_q,T,d] (any strides). Returns O."""
+    _check_inputs(Q, K, V, K_depth, V_depth)
+    if O.device != Q.device or O.dtype != Q.dtype or O.dim() != 4:
+        raise _lib.MoDAShapeError("O must be a 4-D tensor on Q's device with Q's dtype")
+    lib = _lib.load()
+    stream = torch.cuda.current_stream(Q.device).cuda_stream
+    with torch.cuda.device(Q.device):
+        code = lib.moda_fwd_ex(_desc(Q), _desc(K), _desc(V), _desc(K_depth), _desc(V_depth),
+                               _desc(O), int(num_layers), float(scale) if scale else 0.0,
+                               int(chunk_size or 0), _DTYPES[Q.dtype], _KERNELS[kernel],
+                               stream)
+    _lib.check(code, "moda_fwd")
+    return O
+
+
+def moda_plan(Q, K, V, K_depth, V_depth, num_layers: int, kernel: str = "auto") -> str:
+    """Which kernel a call would launch ("tc" or "simt"). Host-only; works on any device."""
+    O_shape = (Q.shape[0], Q.shape[1], Q.shape[2], Q.shape[3])
+    o = _lib.describe(Q.data_ptr(), O_shape, Q.stride())
+    code = _lib.load().moda_fwd_plan(_desc(Q), _desc(K), _desc(V), _desc(K_depth),
+                                     _desc(V_depth), o, int(num_layers), _DTYPES[Q.dtype],
+                                     _KERNELS[kernel])
+    _lib.check(code, "moda_fwd_plan")
+    return {_lib.KERNEL_TC: "tc", _lib.KERNEL_SIMT: "simt"}[code]
+
+
+class _MoDAFunction(torch.autograd.Function):
+    """Forward in libmoda_b200.so. Backward recomputes the attention weights with
+    PyTorch ops on the same CUDA device (not a tuned kernel: the forward is the
+    product here; a fused backward kernel is not built yet)."""
+
+    @staticmethod
+    def forward(ctx, Q, K, V, K_depth, V_depth, num_layers, scale, chunk_size, kernel):
+        O = torch.empty(Q.shape, dtype=Q.dtype, device=Q.device)
+        moda_forward_into(O, Q, K, V, K_depth, V_depth, num_layers, scale, chunk_size, kernel)
+        ctx.save_for_backward(Q, K, V, K_depth, V_depth)
+        ctx.num_layers = num_layers
+        ctx.scale = scale
+        return O
+
+    @staticmethod
+    def backward(ctx, dO):
+        Q, K, V, Kd, Vd = ctx.saved_tensors
+        with torch.enable_grad():
+            ins = [t.detach().float().requires_grad_(True) for t in (Q, K, V, Kd, Vd)]
+            out = _recompute(*ins, ctx.num_layers, ctx.scale)
+            grads = torch.autograd.grad(out, ins, dO.float())
+        return (*[g.to(t.dtype) for g, t in zip(grads, (Q, K, V, Kd, Vd))],
+                None, None, None, None)
+
+
+def _recompute(Q, K, V, Kd, Vd, L, scale):
+    """Differentiable restatement of the forward (fp32, GQA by index, rows [0, T*L) of depth)."""
+    B, H_q, T, d = Q.shape
+    H_k = K.shape[1]
+    G = H_q // H_k
+    s = scale if scale else d ** -0.5
+    Qg = Q.view(B, H_k, G, T, d)
+    s_seq = torch.einsum("bhgtd,bhsd->bhgts", Qg, K) * s
+    causal = torch.ones(T, T, dtype=torch.bool, device=Q.device).triu(1)
+    s_seq = s_seq.masked_fill(causal, float("-inf"))
+    parts = [s_seq]
+    if L > 0:
+        kd = Kd[:, :, :T * L].reshape(B, H_k, T, L, d)
+        s_dep = torch.einsum("bhgtd,bhtld->bhgtl", Qg, kd) * s
+        parts.append(s_dep)
+    w = torch.softmax(torch.cat(parts, dim=-1), dim=-1)
+    out = torch.einsum("bhgts,bhsd->bhgtd", w[..., :T], V)
+    if L > 0:
+        vd = Vd[:, :, :T * L].reshape(B, H_k, T, L, d)
+        out = out + torch.einsum("bhgtl,bhtld->bhgtd", w[..., T:], vd)
+    return out.reshape(B, H_q, T, d)
+
+
+def moda_attention_cuda(Q: Tensor, K: Tensor, V: Tensor, K_depth: Tensor, V_depth: Tensor,
+                        num_layers: int, scale: Optional[float] = None,
+                        chunk_size: Optional[int] = None, *, kernel: str = "auto") -> Tensor:
+    """MoDA attention: fused sequence + depth attention with one combined softmax.
+
+    Args:
+        Q: [B, H_q, T, d] queries. K, V: [B, H_k, T, d]. K_depth, V_depth:
+            [B, H_k, R, d] with R >= T*num_layers; token t's depth rows are
+            [t*L, (t+1)*L) (DepthKVCache layout, moda/cache.py:8-20).
+        num_layers: L, depth rows per token (0 = plain causal attention).
+        scale: softmax scale, default d**-0.5 (moda_naive.py:48-49).
+        chunk_size: accepted for signature parity; the result does not depend on it.
+        kernel: "auto" (default), "tc" or "simt" to force a kernel.
+
+    Returns:
+        [B, H_q, T, d] contiguous tensor of Q's dtype.
+    """
+    if kernel not in _KERNELS:
+        raise ValueError(f"kernel must be one of {sorted(_KERNELS)}")
+    if num_layers is None or int(num_layers) < 0:
+        raise ValueError(f"num_layers must be a non-negative int, got {num_layers}")
+    _check_inputs(Q, K, V, K_depth, V_depth)
+    needs_grad = torch.is_grad_enabled() and any(
+        t.requires_grad for t in (Q, K, V, K_depth, V_depth))
+    if needs_grad:
+        return _MoDAFunction.apply(Q, K, V, K_depth, V_depth, int(num_layers), scale,
+                                   chunk_size, kernel)
+    O = torch.empty(Q.shape, dtype=Q.dtype, device=Q.device)
+    return moda_forward_into(O, Q, K, V, K_depth, V_depth, int(num_layers), scale, chunk_size,
+                             kernel)
+
+
+def depth_append(k_cache: Tensor, v_cache: Tensor, layer_idx: int, k: Tensor, v: Tensor,
+                 num_layers: int, seq_len: int) -> None:
+    """k_cache[:, :, t*L + layer_idx] = k[:, :, t] for t < seq_len (and v); one CUDA launch."""
+    for n, t in (("k_cache", k_cache), ("v_cache", v_cache), ("k", k), ("v", v)):
+        if t.device.type != "cuda":
+            raise RuntimeError(f"depth append runs on CUDA tensors only ({n} is on {t.device})")
+        if t.dim() != 4:
+            raise _lib.MoDAShapeError(f"{n} must be 4-D")
+        if t.dtype != k_cache.dtype:
+            raise TypeError(f"{n} has dtype {t.dtype}, cache has {k_cache.dtype}")
+        if t.device != k_cache.device:
+            raise RuntimeError(f"{n} is on {t.device}, cache on {k_cache.device}")
+    if k_cache.dtype not in _DTYPES:
+        raise TypeError(f"unsupported cache dtype {k_cache.dtype}")
+    lib = _lib.load()
+    stream = torch.cuda.current_stream(k_cache.device).cuda_stream
+    with torch.cuda.device(k_cache.device):
+        code = lib.moda_depth_append(_desc(k), _desc(v), _desc(k_cache), _desc(v_cache),
+                                     int(layer_idx), int(num_layers), int(seq_len),
+                                     _DTYPES[k_cache.dtype], stream)
+    _lib.check(code, "moda_depth_append")
+
+
+def device_status(device=None) -> int:
+    """Read and clear the kernels' timeout status word (0 = no bounded wait expired)."""
+    stream = torch.cuda.current_stream(device).cuda_stream
+    code = _lib.load().moda_device_status(stream)
+    _lib.check(code, "moda_device_status")
+    return code

@@ -1,0 +1,115 @@
+"""C-ABI library: loads, exports what include/moda_b200.h declares, validates and
+plans on the host. No kernel launches (these run without a GPU)."""
+
+import os
+import re
+
+import pytest
+import torch
+
+from moda.kernels import _lib
+from moda.kernels.moda_cuda import moda_plan
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                      "include", "moda_b200.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\*?\s+\*?(moda_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_header_declares_the_entry_points():
+    assert declared_functions() == sorted(_lib.EXPORTED_SYMBOLS)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+    assert lib.moda_version() == 100
+    assert lib.moda_last_error() == b""
+
+
+def _t(shape, dtype=torch.bfloat16, strides=None):
+    x = torch.empty(shape, dtype=dtype)
+    return x if strides is None else x.as_strided(shape, strides)
+
+
+def _plan(B, Hq, Hk, T, d, L, dtype=torch.bfloat16, extra=0, kernel="auto", q=None):
+    Q = q if q is not None else _t((B, Hq, T, d), dtype)
+    K, V = _t((B, Hk, T, d), dtype), _t((B, Hk, T, d), dtype)
+    Kd, Vd = _t((B, Hk, T * L + extra, d), dtype), _t((B, Hk, T * L + extra, d), dtype)
+    return moda_plan(Q, K, V, Kd, Vd, L, kernel=kernel)
+
+
+@pytest.mark.parametrize("d,dtype,expect", [
+    (128, torch.bfloat16, "tc"), (64, torch.bfloat16, "tc"), (64, torch.float16, "tc"),
+    (128, torch.float32, "simt"), (32, torch.bfloat16, "simt"), (256, torch.bfloat16, "simt"),
+])
+def test_plan_by_dtype_and_head_dim(d, dtype, expect):
+    assert _plan(1, 8, 2, 100, d, 4, dtype) == expect
+
+
+@pytest.mark.parametrize("G,expect", [(1, "tc"), (2, "tc"), (4, "tc"), (8, "tc"), (16, "tc"),
+                                      (3, "simt"), (6, "simt")])
+def test_plan_by_group_size(G, expect):
+    assert _plan(1, 2 * G, 2, 64, 128, 2) == expect
+
+
+def test_plan_strided_views_like_moda_attention():
+    # MoDAAttention passes q_proj(x).view(B,T,H,d).transpose(1,2): strides (T*H*d, d, H*d, 1)
+    B, T, H, d = 2, 40, 8, 64
+    q = torch.empty(B, T, H, d, dtype=torch.bfloat16).transpose(1, 2)
+    assert _plan(B, H, 4, T, d, 3, q=q) == "tc"
+    # an innermost stride != 1 can only run on the CUDA-core kernel
+    q2 = torch.empty(B, H, d, T, dtype=torch.bfloat16).transpose(2, 3)
+    assert _plan(B, H, 4, T, d, 3, q=q2) == "simt"
+    with pytest.raises(RuntimeError):
+        _plan(B, H, 4, T, d, 3, q=q2, kernel="tc")
+
+
+def test_plan_oversize_depth_buffer_is_accepted():
+    assert _plan(1, 4, 2, 20, 64, 4, extra=16) == "tc"
+
+
+def test_short_depth_buffer_is_rejected_before_launch():
+    # D1: K_depth with 5 layers of rows but num_layers=6 (reference raises RuntimeError)
+    B, H, Hk, T, d = 1, 8, 4, 64, 64
+    Q = _t((B, H, T, d)); K = _t((B, Hk, T, d)); V = _t((B, Hk, T, d))
+    Kd = _t((B, Hk, T * 5, d)); Vd = _t((B, Hk, T * 5, d))
+    with pytest.raises(RuntimeError, match="rows"):
+        moda_plan(Q, K, V, Kd, Vd, 6)
+    with pytest.raises(ValueError):
+        moda_plan(Q, K, V, Kd, Vd, 6)
+
+
+@pytest.mark.parametrize("bad", ["heads", "head_dim", "batch", "kv_len"])
+def test_shape_mismatches_raise(bad):
+    B, Hq, Hk, T, d, L = 2, 8, 4, 16, 64, 2
+    shapes = dict(Q=(B, Hq, T, d), K=(B, Hk, T, d), V=(B, Hk, T, d), Kd=(B, Hk, T * L, d))
+    if bad == "heads":
+        shapes["K"] = (B, 3, T, d)
+    elif bad == "head_dim":
+        shapes["V"] = (B, Hk, T, 32)
+    elif bad == "batch":
+        shapes["Kd"] = (1, Hk, T * L, d)
+    else:
+        shapes["K"] = (B, Hk, T + 1, d)
+    with pytest.raises(_lib.MoDAShapeError):
+        moda_plan(_t(shapes["Q"]), _t(shapes["K"]), _t(shapes["V"]), _t(shapes["Kd"]),
+                  _t((B, Hk, T * L, d)), L)
+
+
+def test_negative_num_layers_rejected():
+    x = _t((1, 2, 8, 64))
+    with pytest.raises(ValueError):
+        moda_plan(x, x, x, x, x, -1)
+
+
+def test_cpu_tensors_are_refused_by_the_kernel_entry():
+    from moda.kernels import moda_attention_cuda
+    x = torch.zeros(1, 2, 4, 16)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        moda_attention_cuda(x, x, x, torch.zeros(1, 2, 8, 16), torch.zeros(1, 2, 8, 16), 2)

@@ -1,0 +1,225 @@
+"""Parity of the CUDA forward (libmoda_b200.so via its C ABI) with the oracle.
+
+Tolerances:
+  fp32 kernel vs fp32 reference: max|o - ref| / max|ref| <= 1e-4   (FP32_REL_TOL)
+  bf16/f16 kernel vs fp64 oracle on the same rounded inputs: max|o - ref| <= 2e-2 (BF16_ABS_TOL)
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from moda.kernels import moda_attention_cuda, device_status, moda_plan
+from oracle import moda_oracle as orc
+from helpers import (BF16_ABS_TOL, FP32_REL_TOL, golden_cases, max_abs, rel_err,
+                     seeded_inputs)
+
+pytestmark = pytest.mark.gpu
+KERNEL_CASES = golden_cases("kernel")
+
+
+def dev(arrs, dtype):
+    return [torch.from_numpy(np.ascontiguousarray(a)).to("cuda", dtype) for a in arrs]
+
+
+def rounded(arrs, dtype):
+    """The inputs exactly as the kernel sees them, back in float64."""
+    return [torch.from_numpy(np.ascontiguousarray(a)).to(dtype).double().numpy() for a in arrs]
+
+
+def run(args, L, scale=None, chunk=None, kernel="auto"):
+    out = moda_attention_cuda(*args, L, scale, chunk, kernel=kernel)
+    torch.cuda.synchronize()
+    return out.float().cpu().numpy()
+
+
+@pytest.fixture(autouse=True)
+def _no_device_timeouts():
+    yield
+    assert device_status() == 0, "a bounded device wait expired"
+
+
+# ------------------------------------------------------------------ golden vectors
+@pytest.mark.parametrize("name,z,meta", KERNEL_CASES, ids=[c[0] for c in KERNEL_CASES])
+def test_golden_fp32(name, z, meta):
+    arrs = [z[k] for k in ("Q", "K", "V", "K_depth", "V_depth")]
+    out = run(dev(arrs, torch.float32), meta["L"], meta["scale"])
+    ref_key = "out_full" if "out_full" in z.files else \
+        [k for k in z.files if k.startswith("out_")][0]
+    assert rel_err(out, z[ref_key]) <= FP32_REL_TOL, rel_err(out, z[ref_key])
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "f16"])
+@pytest.mark.parametrize("name,z,meta", KERNEL_CASES, ids=[c[0] for c in KERNEL_CASES])
+def test_golden_half(name, z, meta, dtype):
+    arrs = [z[k] for k in ("Q", "K", "V", "K_depth", "V_depth")]
+    ref = orc.moda_attention_naive(*rounded(arrs, dtype), meta["L"], meta["scale"],
+                                   chunk_size=meta["T"])
+    for kernel in ("auto", "simt"):
+        out = run(dev(arrs, dtype), meta["L"], meta["scale"], kernel=kernel)
+        assert max_abs(out, ref) <= BF16_ABS_TOL, (kernel, max_abs(out, ref))
+
+
+def test_golden_c1_runs_the_tensor_core_kernel_in_bf16():
+    z = dict(np.load(__import__("helpers").GOLDEN + "/c1_b1_h4x2_t32_d64_l8.npz"))
+    args = dev([z[k] for k in ("Q", "K", "V", "K_depth", "V_depth")], torch.bfloat16)
+    assert moda_plan(*args, 8) == "tc"
+
+
+# ------------------------------------------------------------------ seeded sweeps vs oracle
+SHAPES = [
+    # B, H_q, H_k, T, d, L
+    (1, 4, 2, 32, 64, 8),
+    (2, 8, 2, 300, 128, 32),
+    (1, 4, 4, 129, 64, 1),
+    (1, 16, 2, 257, 64, 48),
+    (2, 4, 1, 1000, 128, 5),
+    (1, 32, 8, 200, 128, 32),
+    (1, 2, 2, 1, 128, 3),
+    (1, 2, 1, 127, 64, 2),
+    (1, 2, 1, 128, 64, 2),
+    (1, 2, 2, 256, 128, 24),
+    (1, 64, 8, 70, 128, 48),
+    (1, 8, 8, 90, 64, 12),
+    (1, 128, 1, 40, 64, 3),
+]
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=[str(s) for s in SHAPES])
+def test_tc_matches_oracle_bf16(shape):
+    B, Hq, Hk, T, d, L = shape
+    arrs = seeded_inputs(B, Hq, Hk, T, d, L, seed=hash(shape) % 1000)
+    args = dev(arrs, torch.bfloat16)
+    assert moda_plan(*args, L) == "tc"
+    ref = orc.moda_attention_naive(*rounded(arrs, torch.bfloat16), L, chunk_size=64)
+    out = run(args, L, kernel="tc")
+    assert max_abs(out, ref) <= BF16_ABS_TOL, max_abs(out, ref)
+
+
+@pytest.mark.parametrize("shape", [(1, 4, 2, 77, 64, 3), (2, 6, 3, 40, 32, 5), (1, 2, 1, 50, 256, 2),
+                                   (1, 3, 1, 33, 16, 32)])
+def test_simt_fp32_matches_oracle(shape):
+    B, Hq, Hk, T, d, L = shape
+    arrs = seeded_inputs(B, Hq, Hk, T, d, L, seed=11)
+    ref = orc.moda_attention_naive(*arrs, L, chunk_size=16)
+    out = run(dev(arrs, torch.float32), L)
+    assert rel_err(out, ref) <= FP32_REL_TOL
+
+
+# ------------------------------------------------------------------ relational properties
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_causal_invariance(dtype):
+    # reference tests/test_kernel.py:32-44: a later key never changes an earlier row
+    args = dev(seeded_inputs(1, 4, 2, 200, 64, 4, seed=3), dtype)
+    out = moda_attention_cuda(*args, 4)
+    K2 = args[1].clone()
+    K2[:, :, 150] = 999.0
+    out2 = moda_attention_cuda(args[0], K2, *args[2:], 4)
+    assert torch.equal(out[:, :, :150], out2[:, :, :150])
+    assert not torch.equal(out[:, :, 150:], out2[:, :, 150:])
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_depth_isolation(dtype):
+    # reference tests/test_kernel.py:46-59: token t reads only depth rows [t*L, (t+1)*L)
+    L = 3
+    args = dev(seeded_inputs(1, 4, 2, 100, 64, L, seed=4), dtype)
+    out = moda_attention_cuda(*args, L)
+    Kd2 = args[3].clone()
+    Kd2[:, :, 40 * L:41 * L] = 999.0
+    out2 = moda_attention_cuda(*args[:3], Kd2, args[4], L)
+    changed = (out != out2).any(dim=-1).any(dim=0).any(dim=0)
+    assert changed.nonzero().flatten().tolist() == [40]
+
+
+def test_gqa_heads_share_kv():
+    # reference tests/test_gqa.py:51-69
+    args = dev(seeded_inputs(1, 8, 2, 64, 128, 4, seed=5), torch.bfloat16)
+    Q = args[0].clone()
+    Q[:, 1] = Q[:, 0]
+    out = moda_attention_cuda(Q, *args[1:], 4)
+    assert torch.equal(out[:, 0], out[:, 1])
+
+
+@pytest.mark.parametrize("kernel", ["auto", "simt"])
+def test_chunk_size_does_not_change_the_result(kernel):
+    args = dev(seeded_inputs(1, 4, 2, 150, 64, 6, seed=6), torch.bfloat16)
+    base = moda_attention_cuda(*args, 6, kernel=kernel)
+    for C in (None, 1, 7, 64, 128, 4096):
+        assert torch.equal(moda_attention_cuda(*args, 6, chunk_size=C, kernel=kernel), base)
+
+
+def test_deterministic():
+    args = dev(seeded_inputs(2, 8, 2, 333, 128, 32, seed=7), torch.bfloat16)
+    a = moda_attention_cuda(*args, 32)
+    assert all(torch.equal(a, moda_attention_cuda(*args, 32)) for _ in range(3))
+
+
+def test_no_depth_is_causal_attention():
+    B, Hq, Hk, T, d = 1, 8, 2, 200, 128
+    arrs = seeded_inputs(B, Hq, Hk, T, d, 0, seed=8)
+    args = dev(arrs, torch.bfloat16)
+    ref = orc.moda_attention_naive(*rounded(arrs, torch.bfloat16), 0)
+    assert max_abs(run(args, 0), ref) <= BF16_ABS_TOL
+
+
+def test_strided_views_and_oversize_depth():
+    # the layouts MoDAAttention and DepthKVCache.read() hand over (moda/attention.py:77-79,
+    # moda/cache.py:85-88): transposed projections and a prefix view of a larger cache
+    B, T, Hq, Hk, d, L, maxT = 2, 96, 8, 4, 64, 5, 130
+    g = torch.Generator(device="cuda").manual_seed(9)
+    Q = torch.randn(B, T, Hq, d, device="cuda", generator=g).to(torch.bfloat16).transpose(1, 2)
+    K = torch.randn(B, T, Hk, d, device="cuda", generator=g).to(torch.bfloat16).transpose(1, 2)
+    V = torch.randn(B, T, Hk, d, device="cuda", generator=g).to(torch.bfloat16).transpose(1, 2)
+    kc = torch.randn(B, Hk, maxT * L, d, device="cuda", generator=g).to(torch.bfloat16)
+    vc = torch.randn(B, Hk, maxT * L, d, device="cuda", generator=g).to(torch.bfloat16)
+    Kd, Vd = kc[:, :, :T * L], vc[:, :, :T * L]
+    assert not Q.is_contiguous() and not Kd.is_contiguous()
+    assert moda_plan(Q, K, V, Kd, Vd, L) == "tc"
+    out = moda_attention_cuda(Q, K, V, Kd, Vd, L)
+    # the whole cache (rows beyond T*L ignored) gives the same answer
+    assert torch.equal(out, moda_attention_cuda(Q, K, V, kc, vc, L))
+    ref = orc.moda_attention_naive(*[t.double().cpu().numpy() for t in (Q, K, V, Kd, Vd)], L)
+    assert max_abs(out.float().cpu().numpy(), ref) <= BF16_ABS_TOL
+    out_c = moda_attention_cuda(Q.contiguous(), K.contiguous(), V.contiguous(),
+                                Kd.contiguous(), Vd.contiguous(), L)
+    assert torch.equal(out, out_c)
+
+
+def test_write_into_strided_output():
+    from moda.kernels.moda_cuda import moda_forward_into
+    args = dev(seeded_inputs(1, 4, 2, 64, 64, 2, seed=10), torch.bfloat16)
+    ref = moda_attention_cuda(*args, 2)
+    O = torch.zeros(1, 64, 4, 64, dtype=torch.bfloat16, device="cuda").transpose(1, 2)
+    moda_forward_into(O, *args, 2, kernel="simt")
+    assert max_abs(O.float().cpu(), ref.float().cpu()) <= 1e-2
+
+
+def test_short_depth_buffer_raises_like_the_reference():
+    args = dev(seeded_inputs(1, 8, 4, 64, 64, 5, seed=12), torch.bfloat16)
+    with pytest.raises(RuntimeError):
+        moda_attention_cuda(*args, 6)
+
+
+# ------------------------------------------------------------------ full benchmark sizes
+@pytest.mark.slow
+def test_kernel_only_benchmark_config_sampled_rows():
+    # B=4 H_q=32 H_k=8 T=8192 d=128 L=32 bf16: spot rows against the oracle
+    B, Hq, Hk, T, d, L = 4, 32, 8, 8192, 128, 32
+    g = torch.Generator(device="cuda").manual_seed(2)
+    mk = lambda *s: torch.randn(*s, device="cuda", generator=g, dtype=torch.bfloat16)
+    Q, K, V = mk(B, Hq, T, d), mk(B, Hk, T, d), mk(B, Hk, T, d)
+    Kd, Vd = mk(B, Hk, T * L, d), mk(B, Hk, T * L, d)
+    out = moda_attention_cuda(Q, K, V, Kd, Vd, L, chunk_size=64)
+    assert torch.isfinite(out).all()
+    rng = np.random.default_rng(0)
+    rows = [(0, 0, 0), (B - 1, Hq - 1, T - 1), (1, 5, 4095), (2, 17, 128), (3, 31, 127)]
+    rows += [(int(rng.integers(B)), int(rng.integers(Hq)), int(rng.integers(T))) for _ in range(27)]
+    G = Hq // Hk
+    for (b, h, t) in rows:
+        hk = h // G
+        ref = orc.moda_row(Q[b, h, t].cpu().double().numpy(), K[b, hk, :t + 1].cpu().double().numpy(),
+                           V[b, hk, :t + 1].cpu().double().numpy(),
+                           Kd[b, hk, t * L:(t + 1) * L].cpu().double().numpy(),
+                           Vd[b, hk, t * L:(t + 1) * L].cpu().double().numpy(), d ** -0.5)
+        assert max_abs(out[b, h, t].float().cpu().numpy(), ref) <= BF16_ABS_TOL, (b, h, t)

@@ -1,0 +1,193 @@
+"""MoDAAttention / DepthKVCache / MoDAModel on CUDA against the reference's outputs.
+
+The golden files hold the reference modules' weights, inputs and outputs (CPU,
+fp32). Loading the same weights into this package's modules must reproduce
+them: fp32 within 1e-4 relative (FP32_REL_TOL).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from moda import DepthKVCache, MoDAAttention, MoDAConfig, MoDAModel, MoDATransformerBlock
+from moda.kernels import device_status
+from helpers import FP32_REL_TOL, load_golden, max_abs, rel_err
+
+pytestmark = pytest.mark.gpu
+
+
+def weights(z):
+    return {k[2:]: torch.from_numpy(z[k]) for k in z.files if k.startswith("w.")}
+
+
+@pytest.fixture(autouse=True)
+def _no_device_timeouts():
+    yield
+    assert device_status() == 0
+
+
+def test_attention_module_matches_reference():
+    z, meta = load_golden("module_attention")
+    attn = MoDAAttention(MoDAConfig(**meta["config"]))
+    attn.load_state_dict(weights(z))
+    attn = attn.cuda().eval()
+    x, Kd, Vd = (torch.from_numpy(z[k]).cuda() for k in ("x", "K_depth", "V_depth"))
+    with torch.no_grad():
+        out, kw, vw = attn(x, Kd, Vd)
+    assert rel_err(out.cpu().numpy(), z["out"]) <= FP32_REL_TOL
+    assert max_abs(kw.cpu().numpy(), z["k_write"]) < 1e-5
+    assert max_abs(vw.cpu().numpy(), z["v_write"]) < 1e-5
+
+
+@pytest.mark.parametrize("name", ["model_postnorm", "model_prenorm"])
+def test_model_matches_reference(name):
+    # includes the reference's depth addressing quirk: 2N cache slots per token
+    # addressed with L = N (moda/model.py:143-151, moda/attention.py:90)
+    z, meta = load_golden(name)
+    model = MoDAModel(MoDAConfig(**meta["config"]))
+    model.load_state_dict(weights(z))
+    model = model.cuda().eval()
+    with torch.no_grad():
+        out = model(torch.from_numpy(z["x"]).cuda())
+    assert rel_err(out.cpu().numpy(), z["out"]) <= FP32_REL_TOL
+
+
+def test_depth_cache_layout_matches_reference():
+    z, meta = load_golden("cache_write")
+    B, T, L, H, d = meta["B"], meta["T"], meta["L"], meta["H_k"], meta["d"]
+    cache = DepthKVCache(B, T, L, H, d, device="cuda")
+    for layer in meta["order"]:
+        cache.write(layer, torch.from_numpy(z[f"k{layer}"]).cuda(),
+                    torch.from_numpy(z[f"v{layer}"]).cuda())
+    K, V = cache.read(seq_len=T)
+    assert np.array_equal(K.cpu().numpy(), z["k_cache"])
+    assert np.array_equal(V.cpu().numpy(), z["v_cache"])
+    assert tuple(cache.read(seq_len=3)[0].shape) == tuple(z["partial_shape"])
+    cache.reset()
+    assert (cache.read(seq_len=T)[0] == 0).all()
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_depth_cache_strided_sources_bit_exact(dtype):
+    # sources are transposed projection views (moda/model.py:79-82)
+    B, T, H, d, L, maxT = 2, 37, 4, 64, 6, 50
+    cache = DepthKVCache(B, maxT, L, H, d, device="cuda", dtype=dtype)
+    ref_k = torch.zeros(B, H, maxT * L, d, dtype=dtype)
+    for layer in (0, 3, 5):
+        k = torch.randn(B, T, H, d, device="cuda").to(dtype).transpose(1, 2)
+        v = torch.randn(B, T, H, d, device="cuda").to(dtype).transpose(1, 2)
+        cache.write(layer, k, v, seq_len=T)
+        ref_k[:, :, layer:T * L:L] = k.cpu()
+        assert torch.equal(cache.v_cache[:, :, layer:T * L:L].cpu(), v.cpu())
+    assert torch.equal(cache.k_cache.cpu(), ref_k)
+
+
+def test_depth_cache_append_validates_layer_index():
+    cache = DepthKVCache(1, 8, 3, 2, 16, device="cuda")
+    k = torch.zeros(1, 2, 8, 16, device="cuda")
+    with pytest.raises(ValueError):
+        cache.write(3, k, k)
+
+
+# ---- the reference's own module/model tests, on CUDA (tests/test_attention.py, test_model.py)
+def _cfg(**kw):
+    d = dict(d_model=64, num_heads=4, num_kv_heads=2, num_layers=3)
+    d.update(kw)
+    return MoDAConfig(**d)
+
+
+def test_forward_no_depth_and_with_depth_shapes():
+    cfg = _cfg()
+    attn = MoDAAttention(cfg).cuda()
+    x = torch.randn(2, 8, cfg.d_model, device="cuda")
+    out, kw, vw = attn(x)
+    assert out.shape == (2, 8, 64) and kw.shape == (2, 2, 8, 16) and vw.shape == (2, 2, 8, 16)
+    Kd = torch.randn(2, 2, 8 * 4, 16, device="cuda")
+    out2, _, _ = attn(x, Kd, Kd.clone())
+    assert out2.shape == (2, 8, 64)
+
+
+def test_no_depth_path_equals_sdpa():
+    cfg = _cfg(num_heads=8, num_kv_heads=2, d_model=512)
+    attn = MoDAAttention(cfg).cuda().eval()
+    x = torch.randn(2, 40, 512, device="cuda")
+    with torch.no_grad():
+        out, _, _ = attn(x)
+        B, T, _ = x.shape
+        Q = attn.q_proj(x).view(B, T, 8, 64).transpose(1, 2)
+        K = attn.k_proj(x).view(B, T, 2, 64).transpose(1, 2).repeat_interleave(4, 1)
+        V = attn.v_proj(x).view(B, T, 2, 64).transpose(1, 2).repeat_interleave(4, 1)
+        ref = torch.nn.functional.scaled_dot_product_attention(Q, K, V, is_causal=True)
+        ref = attn.o_proj(ref.transpose(1, 2).reshape(B, T, 512))
+    assert rel_err(out.cpu().numpy(), ref.cpu().numpy()) <= FP32_REL_TOL
+
+
+def test_depth_changes_output():
+    cfg = _cfg()
+    attn = MoDAAttention(cfg).cuda().eval()
+    x = torch.randn(1, 4, 64, device="cuda")
+    with torch.no_grad():
+        a, _, _ = attn(x)
+        b, _, _ = attn(x, torch.randn(1, 2, 12, 16, device="cuda"),
+                       torch.randn(1, 2, 12, 16, device="cuda"))
+    assert not torch.allclose(a, b, atol=1e-3)
+
+
+def test_gradients_reach_inputs_and_depth():
+    cfg = _cfg()
+    attn = MoDAAttention(cfg).cuda()
+    x = torch.randn(1, 4, 64, device="cuda", requires_grad=True)
+    Kd = torch.randn(1, 2, 12, 16, device="cuda", requires_grad=True)
+    Vd = torch.randn(1, 2, 12, 16, device="cuda", requires_grad=True)
+    out, _, _ = attn(x, Kd, Vd)
+    out.sum().backward()
+    for t in (x, Kd, Vd):
+        assert t.grad is not None and torch.isfinite(t.grad).all()
+
+
+def test_kernel_gradients_match_oracle_math():
+    from moda.kernels import moda_attention_cuda
+    torch.manual_seed(0)
+    ins = [torch.randn(s, device="cuda", dtype=torch.float64 if False else torch.float32,
+                       requires_grad=True)
+           for s in [(1, 4, 6, 8), (1, 2, 6, 8), (1, 2, 6, 8), (1, 2, 18, 8), (1, 2, 18, 8)]]
+    out = moda_attention_cuda(*ins, 3)
+    g = torch.randn_like(out)
+    grads = torch.autograd.grad(out, ins, g)
+    # finite-difference check on one coordinate of each input
+    eps = 1e-3
+    for i, gr in enumerate(grads):
+        x = ins[i].detach().clone()
+        idx = (0, 1, 2, 3)
+        xp, xm = x.clone(), x.clone()
+        xp[idx] += eps
+        xm[idx] -= eps
+        args_p = [t.detach() for t in ins]
+        args_m = [t.detach() for t in ins]
+        args_p[i], args_m[i] = xp, xm
+        fd = ((moda_attention_cuda(*args_p, 3) - moda_attention_cuda(*args_m, 3)) * g).sum() / (2 * eps)
+        assert abs(fd.item() - gr[idx].item()) < 2e-2 * max(1.0, abs(fd.item()))
+
+
+def test_block_and_model_shapes_and_backward():
+    cfg = _cfg()
+    block = MoDATransformerBlock(cfg, layer_idx=0).cuda()
+    cache = DepthKVCache(2, 8, cfg.num_layers * 2, 2, 16, device="cuda")
+    out = block(torch.randn(2, 8, 64, device="cuda"), depth_cache=cache)
+    assert out.shape == (2, 8, 64) and not (cache.read(seq_len=8)[0] == 0).all()
+    model = MoDAModel(_cfg(num_layers=2, max_seq_len=16)).cuda()
+    x = torch.randn(1, 4, 64, device="cuda", requires_grad=True)
+    model(x).sum().backward()
+    assert x.grad is not None
+    ids = torch.randint(0, 16, (2, 8), device="cuda")
+    assert model(ids).shape == (2, 8, 64)
+    m2 = MoDAModel(_cfg(num_layers=2, max_seq_len=16, post_norm=False)).cuda()
+    assert m2(torch.randn(1, 4, 64, device="cuda")).shape == (1, 4, 64)
+
+
+def test_model_bf16_runs_the_tensor_core_kernel():
+    cfg = MoDAConfig(d_model=512, num_heads=8, num_kv_heads=4, num_layers=2, max_seq_len=256)
+    model = MoDAModel(cfg).cuda().to(torch.bfloat16).eval()
+    with torch.no_grad():
+        out = model(torch.randn(2, 200, 512, device="cuda", dtype=torch.bfloat16))
+    assert torch.isfinite(out).all()

@@ -1,0 +1,99 @@
+"""The oracle (oracle/moda_oracle.py) against the reference's own outputs.
+
+The golden fixtures in tests/golden/ were produced by running the reference
+implementation (moda_attention_naive, DepthKVCache) on CPU in fp32; see
+tests/golden/make_golden.py. These tests pin the numpy restatement to them.
+"""
+
+import numpy as np
+import pytest
+
+from oracle import moda_oracle as orc
+from helpers import golden_cases, load_golden, max_abs, seeded_inputs
+
+KERNEL_CASES = golden_cases("kernel")
+
+
+@pytest.mark.parametrize("name,z,meta", KERNEL_CASES, ids=[c[0] for c in KERNEL_CASES])
+def test_oracle_matches_reference_outputs(name, z, meta):
+    args = [z[k] for k in ("Q", "K", "V", "K_depth", "V_depth")]
+    checked = 0
+    for C in meta["chunk_sizes"]:
+        key = "full" if C is None else f"c{C}"
+        if "err_" + key in z.files:
+            # the reference raised for this form; so does the restatement
+            with pytest.raises(ValueError):
+                orc.moda_attention_naive(*args, meta["L"], meta["scale"], C)
+            continue
+        ref = z["out_" + key]
+        out = orc.moda_attention_naive(*args, meta["L"], meta["scale"], C)
+        # reference ran in fp32; the oracle runs in fp64
+        assert max_abs(out, ref) < 2e-5, (name, key, max_abs(out, ref))
+        checked += 1
+    assert checked >= 1
+
+
+def test_golden_c1_is_the_seeded_benchmark_case():
+    z, meta = load_golden("c1_b1_h4x2_t32_d64_l8")
+    assert (meta["B"], meta["H_q"], meta["H_k"], meta["T"], meta["d"], meta["L"], meta["seed"]) == \
+        (1, 4, 2, 32, 64, 8, 0)
+    assert z["K_depth"].shape == (1, 2, 256, 64)
+
+
+def test_oracle_fp32_mode_matches_fp64():
+    args = seeded_inputs(1, 4, 2, 24, 32, 3, seed=5)
+    a = orc.moda_attention_naive(*args, 3, chunk_size=8, dtype=np.float32)
+    b = orc.moda_attention_naive(*args, 3, chunk_size=8)
+    assert a.dtype == np.float32 and max_abs(a, b) < 1e-5
+
+
+@pytest.mark.parametrize("C", [1, 3, 5, 16, 64])
+def test_oracle_chunk_invariance(C):
+    args = seeded_inputs(1, 2, 1, 13, 16, 4, seed=6)
+    full = orc.moda_attention_naive(*args, 4)
+    assert max_abs(orc.moda_attention_naive(*args, 4, chunk_size=C), full) < 1e-12
+
+
+def test_oracle_rows_match_full():
+    args = seeded_inputs(2, 4, 2, 19, 16, 5, seed=7)
+    full = orc.moda_attention_naive(*args, 5)
+    rows = [(0, 0, 0), (1, 3, 18), (0, 2, 7), (1, 1, 11)]
+    got = orc.moda_rows(*args, 5, rows)
+    for i, (b, h, t) in enumerate(rows):
+        assert max_abs(got[i], full[b, h, t]) < 1e-12
+
+
+def test_oracle_depth_rows_short_raises():
+    # D1: a depth buffer with fewer than T*L rows is an error in the reference.
+    Q, K, V, Kd, Vd = seeded_inputs(1, 2, 2, 8, 16, 3, seed=8)
+    with pytest.raises(ValueError):
+        orc.moda_attention_naive(Q, K, V, Kd[:, :, :20], Vd[:, :, :20], 3, chunk_size=4)
+
+
+def test_oracle_causal_and_depth_isolation():
+    # reference tests/test_kernel.py:32-59, restated on the oracle
+    Q, K, V, Kd, Vd = seeded_inputs(1, 1, 1, 4, 8, 3, seed=9)
+    out = orc.moda_attention_naive(Q, K, V, Kd, Vd, 3)
+    K2 = K.copy(); K2[0, 0, 2] = 999.0
+    Kd2 = Kd.copy(); Kd2[0, 0, 6:9] = 999.0
+    assert max_abs(orc.moda_attention_naive(Q, K2, V, Kd, Vd, 3)[:, :, 0], out[:, :, 0]) == 0
+    assert max_abs(orc.moda_attention_naive(Q, K, V, Kd2, Vd, 3)[:, :, 0], out[:, :, 0]) == 0
+
+
+def test_depth_cache_write_restatement():
+    z, meta = load_golden("cache_write")
+    B, T, L, H, d = meta["B"], meta["T"], meta["L"], meta["H_k"], meta["d"]
+    kc = np.zeros((B, H, T * L, d), np.float32)
+    vc = np.zeros_like(kc)
+    for layer in meta["order"]:
+        orc.depth_cache_write(kc, vc, layer, z[f"k{layer}"], z[f"v{layer}"], L)
+    assert max_abs(kc, z["k_cache"]) == 0 and max_abs(vc, z["v_cache"]) == 0
+    assert tuple(z["partial_shape"]) == (B, H, 3 * L, d)
+
+
+def test_roofline_formulas():
+    # kernel-only benchmark configuration: B=4 H_q=32 H_k=8 T=8192 d=128 L=32 bf16
+    f = orc.flops(4, 32, 8192, 128, 32)
+    by = orc.hbm_bytes(4, 32, 8, 8192, 128, 32, 2)
+    assert abs(f / 1e12 - 2.2165) < 1e-3
+    assert abs(by / 1e9 - 4.966) < 1e-3
