@@ -39,6 +39,10 @@ WORKLOADS = {
     "kernel": dict(B=4, Hq=32, Hk=8, T=8192, d=128, L=32, chunk=64, seed=2,
                    desc="kernel-only fused MoDA forward, bf16 fp32-accumulate: "
                         "B=4 H_q=32 H_k=8 T=8192 d=128 L=32 chunk_size=64 per GPU"),
+    # one quarter of the kernel-only workload (B=1): same per-unit shape, for ncu captures
+    "kernel-b1": dict(B=1, Hq=32, Hk=8, T=8192, d=128, L=32, chunk=64, seed=2,
+                      desc="kernel-only fused MoDA forward, bf16: B=1 H_q=32 H_k=8 T=8192 d=128 "
+                           "L=32 chunk_size=64 (profiling size)"),
     "scaling": dict(B=16, Hq=64, Hk=8, T=16384, d=128, L=48, chunk=128, seed=4,
                     desc="multi-GPU fused MoDA forward, bf16: B=16 H_q=64 H_k=8 T=16384 d=128 "
                          "L=48 chunk_size=128, batch split over GPUs"),
@@ -165,7 +169,7 @@ def run_reference(args, wl):
     line = {"impl": "reference", "metric": METRIC, "value": tflops, "unit": "TFLOP/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": sec * 1e3, "higher_is_better": True,
-            "scaling": "weak" if args.workload == "kernel" else "strong", "vs_baseline": None,
+            "scaling": "strong" if args.workload == "scaling" else "weak", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic N(0,1)",
             "config": {"workload": wl["desc"], "sample": "one (batch, kv-head) unit, first 2048 tokens"},
             "cpu_baseline": {"value": tflops, "unit": "TFLOP/s", "cores": threads, "kind": "port",
@@ -224,7 +228,7 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
 
     # shard: weak scaling gives every rank its own 4-batch; strong scaling splits 16 batches
-    if args.workload == "kernel":
+    if args.workload != "scaling":
         b_lo, b_hi = rank * wl["B"], (rank + 1) * wl["B"]
         B_global = wl["B"] * world
     else:
@@ -340,7 +344,7 @@ def main():
     line = {
         "metric": METRIC, "value": tflops, "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
-        "higher_is_better": True, "scaling": "weak" if args.workload == "kernel" else "strong",
+        "higher_is_better": True, "scaling": "strong" if args.workload == "scaling" else "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic N(0,1), seeded per batch",
         "config": {"workload": wl["desc"], "global_batch": B_global, "H_q": Hq, "H_k": Hk,
                    "seq_len": T, "head_dim": d, "num_layers": L, "chunk_size": C,

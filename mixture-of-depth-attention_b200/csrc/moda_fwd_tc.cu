@@ -4,40 +4,61 @@
 //   out = softmax({scale*q.k_j : j <= t} U {scale*q.kd_{t*L+l} : l < L}) . [V ; V_depth]
 // with KV head h / G. One online softmax covers both score sets.
 //
-// Tiling.
+// Work decomposition.
 //   * A query tile is 128 rows of one (batch, KV head): n = 128/G tokens x the G
 //     query heads of that KV head, token-major (row = token_local*G + head). The
 //     TMA box (64, G, n) over the [d, H_q, T, B] view builds it, so every K/V
 //     tile is used once by all G heads of its group -- GQA without
 //     repeat_interleave.
-//   * A CTA owns two consecutive query tiles (A, B) of the same (b, KV head) and
-//     ping-pongs them on the tensor core: while softmax warpgroup A works on
-//     S_A, the tensor core runs tile B's MMAs, and vice versa.
-//   * Each tile walks a list of 128-row key blocks:
-//       - depth blocks: rows [t0*L + 128i, +128) of K_depth/V_depth, exactly the
-//         rows of the tile's own tokens (chunk-aware: a tile of n tokens touches
-//         n*L depth rows), masked so row (token t) keeps rows t*L..t*L+L-1;
-//       - causal sequence blocks 0..ceil((t0+n)/128)-1, masked on the diagonal.
-//     Both kinds go through the same TMA ring and the same two MMAs
-//     (S = Q K^T, O += P V), i.e. the depth phase of the paper's algorithm
-//     (group-aware indexing, depth mask floor(row/G) == floor(j/L)).
+//   * A work item is a pair of consecutive query tiles (A, B) of one (b, KV head).
+//     The kernel is persistent: one CTA per SM walks the items heaviest first
+//     (most causal blocks first) with a fixed stride, so the producer already
+//     streams the next item while the current one drains.
+//   * Each item walks one list of 128-row key blocks shared by both tiles:
+//       - causal sequence blocks j = 0..S-1 (keys [128j, 128j+128)), masked on the
+//         diagonal; both tiles read the same K/V fill;
+//       - depth blocks k = 0..D-1: rows [t0*L + 128k, +128) of K_depth/V_depth,
+//         i.e. only the rows of the tile's own tokens (chunk-aware: a tile of n
+//         tokens touches n*L depth rows), masked so a row of token t keeps rows
+//         t*L..t*L+L-1 (the paper's depth mask floor(row/G) == floor(j/L));
+//     depth blocks are spread evenly between the causal blocks so the HBM-heavy
+//     depth stream overlaps the compute-heavy causal part.
+//   * Every block goes through the same two MMAs, S = Q K^T (A and B from shared
+//     memory) and O += P V (P from tensor memory), and the same online softmax.
 //
-// Warp roles (320 threads):
-//   warps 0-3  softmax + correction + epilogue for tile A (thread = TMEM lane = row)
-//   warps 4-7  the same for tile B
-//   warp  8    TMA producer (Q tiles, then the K/V block ring)
-//   warp  9    TMEM allocator and single-thread tcgen05.mma issuer
+// Warp roles (640 threads = 5 warpgroups):
+//   warps 0-7   softmax for tile A: warp w covers TMEM lane quarter w%4 (32 rows) and
+//               score columns [64*(w/4), +64); the two warps of a quarter trade row
+//               maxima and sums through shared memory (one named barrier per pair)
+//   warps 8-15  the same for tile B
+//   warp  16    TMA producer (Q tiles, then the K/V block ring)
+//   warp  17    TMEM allocator and tcgen05.mma issuer for tile A (one thread)
+//   warp  18    tcgen05.mma issuer for tile B (one thread)
+//   warp  19    idle
+// Two softmax warps per tile and lane quarter keep the MUFU (one ex2 per score)
+// and the tensor core busy at the same time: a single warp per quarter is
+// latency-bound. One MMA issuer per tile keeps each tile's barrier latencies off
+// the other tile's critical path; an issuer checks the ring slots of its next
+// MMAs while the softmax of the current block is still running.
+// Registers: launched at 96 per thread; the producer/MMA warpgroup gives back to
+// 56 and the four softmax warpgroups grow to 104 (4*128*104 + 128*56 <= 640*96).
 //
 // TMEM (512 columns): S_A [0,128) S_B [128,256) O_A [256,256+d) O_B [256+d,256+2d).
-// P (bf16/f16) is written into the upper 64 columns of S and fed to the PV MMA
-// straight from TMEM (A operand in tensor memory), so P never touches shared memory.
+// P (16-bit) is written into the upper 64 columns of S and fed to the PV MMA
+// straight from TMEM, so P never touches shared memory.
 #include "moda_internal.h"
 
 #include <cstdio>
 
 namespace moda {
 
-constexpr int kThreads = 320;
+constexpr int kThreads = 640;
+constexpr int kLaunchRegs = 96;    // 65536 / 640 rounded down to 8, enforced on the host
+constexpr int kSoftmaxRegs = 104;
+constexpr int kProducerRegs = 56;
+static_assert(4 * 128 * kSoftmaxRegs + 128 * kProducerRegs <= kThreads * kLaunchRegs,
+              "register split exceeds the launch allocation");
+constexpr int kWarpProducer = 16, kWarpMmaA = 17, kWarpMmaB = 18;
 constexpr int kBM = 128;  // query rows per tile
 constexpr int kBN = 128;  // key rows per block
 
@@ -45,14 +66,18 @@ template <int HD>
 struct TcCfg {
     static constexpr int kTileBytes = kBM * HD * 2;       // one 128 x HD 16-bit tile
     static constexpr int kColBlocks = HD / 64;            // 128-byte swizzle atoms across d
-    static constexpr int kStages = (HD == 128) ? 4 : 8;   // K/V ring depth
+    static constexpr int kStages = (HD == 128) ? 4 : 10;  // K/V ring depth
     static constexpr int kQOff = 0;
     static constexpr int kRingOff = 2 * kTileBytes;
     static constexpr int kBarOff = kRingOff + kStages * kTileBytes;
-    // barriers: q_full[2], s_full[2], p_full[2], o_done[2], end, slot_full[S], slot_empty[S]
-    static constexpr int kNumBars = 9 + 2 * kStages;
+    // barriers: q_full[2] q_empty[2] s_full[2] p_full[2] o_done[2] o_free[2] end[2],
+    //           slot_full[S] slot_empty_A[S] slot_empty_B[S]
+    static constexpr int kNumBars = 14 + 3 * kStages;
     static constexpr int kMiscOff = kBarOff + kNumBars * 8;
-    static constexpr int kSmemBytes = kMiscOff + 64 + 1024;  // + alignment slack
+    // row-max exchange [tile][block parity][half][row] and row-sum exchange [tile][half][row]
+    static constexpr int kXmaxOff = (kMiscOff + 48 + 15) & ~15;
+    static constexpr int kXsumOff = kXmaxOff + 2 * 2 * 2 * 128 * 4;
+    static constexpr int kSmemBytes = kXsumOff + 2 * 2 * 128 * 4 + 1024;  // + alignment slack
     static constexpr uint32_t kTmemCols = 512;
     static constexpr uint32_t kOCol = 256;
 };
@@ -79,31 +104,65 @@ __device__ __forceinline__ TileInfo tile_info(const TcParams& p, int pair, int x
     return ti;
 }
 
-// Per step s of a tile: which block. Depth blocks first, then causal blocks.
-__device__ __forceinline__ bool is_depth(const TileInfo& ti, int s) { return s < ti.ndep; }
-
-// Ring bookkeeping shared by producer and consumer: the blocks of step s are
-// filled in the order K_A, K_B, V_A, V_B, where K_B / V_B are skipped when both
-// tiles read the same causal block (then one fill serves both).
-struct StepSlots {
-    bool hasA, hasB, shared;
-    uint32_t kA, kB, vA, vB;  // fill indices
-    uint32_t nfill;
+struct Item {
+    int b, hk;
+    TileInfo t[2];
+    int S, D;  // causal / depth blocks of the item (max over its tiles)
+    __device__ int nsteps() const { return S + D; }
 };
 
-__device__ __forceinline__ StepSlots step_slots(const TileInfo& A, const TileInfo& Bt, int s,
-                                                uint32_t base) {
-    StepSlots r;
-    r.hasA = s < A.len();
-    r.hasB = s < Bt.len();
-    r.shared = r.hasA && r.hasB && !is_depth(A, s) && !is_depth(Bt, s) &&
-               (s - A.ndep) == (s - Bt.ndep);
+__device__ __forceinline__ Item item_info(const TcParams& p, int item) {
+    Item it;
+    const int bh_count = p.B * p.Hk;
+    const int pair = p.num_pairs - 1 - item / bh_count;  // heaviest pairs first
+    const int bh = item % bh_count;
+    it.b = bh / p.Hk;
+    it.hk = bh % p.Hk;
+    it.t[0] = tile_info(p, pair, 0);
+    it.t[1] = tile_info(p, pair, 1);
+    it.S = max(it.t[0].nseq, it.t[1].nseq);
+    it.D = max(it.t[0].ndep, it.t[1].ndep);
+    return it;
+}
+
+// One step of an item's block list. Depth block k is placed before causal block j
+// when k/D <= j/S, which spreads the D depth blocks evenly over the S causal ones.
+struct Step {
+    bool dep;
+    int idx;
+    bool has[2];
+};
+
+struct StepWalker {
+    int S, D, j, k;
+    __device__ StepWalker(const Item& it) : S(it.S), D(it.D), j(0), k(0) {}
+    __device__ Step next(const Item& it) {
+        Step st;
+        st.dep = k < D && (j >= S || static_cast<long long>(k) * S <= static_cast<long long>(j) * D);
+        st.idx = st.dep ? k++ : j++;
+        for (int x = 0; x < 2; ++x)
+            st.has[x] = st.dep ? st.idx < it.t[x].ndep : st.idx < it.t[x].nseq;
+        return st;
+    }
+};
+
+// Ring fills of one step, in fill order K_A, K_B, V_A, V_B; a causal block read
+// by both tiles is filled once.
+struct Fills {
+    bool shared;
+    uint32_t k[2], v[2], n;
+};
+
+__device__ __forceinline__ Fills step_fills(const Step& st, uint32_t base) {
+    Fills r;
+    r.shared = !st.dep && st.has[0] && st.has[1];
     uint32_t f = base;
-    if (r.hasA) r.kA = f++;
-    if (r.hasB) r.kB = r.shared ? r.kA : f++;
-    if (r.hasA) r.vA = f++;
-    if (r.hasB) r.vB = r.shared ? r.vA : f++;
-    r.nfill = f - base;
+    r.k[0] = r.k[1] = r.v[0] = r.v[1] = 0;
+    if (st.has[0]) r.k[0] = f++;
+    if (st.has[1]) r.k[1] = r.shared ? r.k[0] : f++;
+    if (st.has[0]) r.v[0] = f++;
+    if (st.has[1]) r.v[1] = r.shared ? r.v[0] : f++;
+    r.n = f - base;
     return r;
 }
 
@@ -118,309 +177,485 @@ __global__ void __launch_bounds__(kThreads, 1) moda_fwd_tc_kernel(const __grid_c
     const uint32_t sRing = sbase + Cfg::kRingOff;
     const uint32_t bar0 = sbase + Cfg::kBarOff;
     auto q_full = [&](int x) { return bar0 + 8u * x; };
-    auto s_full = [&](int x) { return bar0 + 8u * (2 + x); };
-    auto p_full = [&](int x) { return bar0 + 8u * (4 + x); };
-    auto o_done = [&](int x) { return bar0 + 8u * (6 + x); };
-    const uint32_t end_bar = bar0 + 8u * 8;
-    auto slot_full = [&](uint32_t i) { return bar0 + 8u * (9 + i); };
-    auto slot_empty = [&](uint32_t i) { return bar0 + 8u * (9 + Cfg::kStages + i); };
+    auto q_empty = [&](int x) { return bar0 + 8u * (2 + x); };
+    auto s_full = [&](int x) { return bar0 + 8u * (4 + x); };
+    auto p_full = [&](int x) { return bar0 + 8u * (6 + x); };
+    auto o_done = [&](int x) { return bar0 + 8u * (8 + x); };
+    auto o_free = [&](int x) { return bar0 + 8u * (10 + x); };
+    auto end_bar = [&](int x) { return bar0 + 8u * (12 + x); };
+    auto slot_full = [&](uint32_t i) { return bar0 + 8u * (14 + i); };
+    // released by tile x's issuer once its MMAs reading the slot have completed
+    auto slot_empty = [&](int x, uint32_t i) { return bar0 + 8u * (14 + (1 + x) * Cfg::kStages + i); };
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + Cfg::kMiscOff);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Cfg::kMiscOff + 8);
+    // Fills whose TMA loads the producer has started. An issuer looks at a slot's
+    // barrier only for an issued fill: then the slot's previous fill has landed
+    // and been released, so the barrier is exactly at this fill's phase (the
+    // 1-bit parity cannot alias a fill two phases old).
+    volatile uint32_t* issued = reinterpret_cast<volatile uint32_t*>(smem + Cfg::kMiscOff + 16);
+    // Exponential-phase turns of the two tiles: 8 increments (one per softmax warp) per
+    // block whose exponentials are done. A tile starts the exponentials of a block once
+    // the other tile has finished every block that precedes it in the item's step order,
+    // so the two tiles take turns on the MUFU while the tensor core runs the other tile.
+    // Purely a scheduling hint: the result does not depend on it.
+    uint32_t* exp_turns = reinterpret_cast<uint32_t*>(smem + Cfg::kMiscOff + 24);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
-    // heavy pairs (more causal blocks) first
-    const int bh_count = p.B * p.Hk;
-    const int pair = p.num_pairs - 1 - static_cast<int>(blockIdx.x) / bh_count;
-    const int bh = static_cast<int>(blockIdx.x) % bh_count;
-    const int b = bh / p.Hk;
-    const int hk = bh % p.Hk;
-    const TileInfo tA = tile_info(p, pair, 0);
-    const TileInfo tB = tile_info(p, pair, 1);
-    const int nsteps = max(tA.len(), tB.len());
-
     if (threadIdx.x == 0) {
-        for (int i = 0; i < 8; ++i) mbar_init(bar0 + 8u * i, (i == 4 || i == 5) ? kBM : 1);
-        mbar_init(end_bar, 1);
+        for (int x = 0; x < 2; ++x) {
+            mbar_init(q_full(x), 1);
+            mbar_init(q_empty(x), 1);
+            mbar_init(s_full(x), 1);
+            mbar_init(p_full(x), 2 * kBM);
+            mbar_init(o_done(x), 1);
+            mbar_init(o_free(x), 2 * kBM);
+        }
+        mbar_init(end_bar(0), 1);
+        mbar_init(end_bar(1), 1);
         for (int i = 0; i < Cfg::kStages; ++i) {
             mbar_init(slot_full(i), 1);
-            mbar_init(slot_empty(i), 1);
+            mbar_init(slot_empty(0, i), 1);
+            mbar_init(slot_empty(1, i), 1);
         }
         *abort_flag = 0;
+        *issued = 0;
+        exp_turns[0] = 0;
+        exp_turns[1] = 0;
         fence_barrier_init();
     }
-    if (warp == 9) {
+    if (warp == kWarpMmaA) {
         tmem_alloc(smem_u32(tmem_holder), Cfg::kTmemCols);
         tmem_relinquish();
     }
-    if (warp == 8 && lane == 0) {
+    if (warp == kWarpProducer && lane == 0) {
         tma_prefetch_desc(&p.tm_q);
         tma_prefetch_desc(&p.tm_k);
         tma_prefetch_desc(&p.tm_v);
         tma_prefetch_desc(&p.tm_kd);
         tma_prefetch_desc(&p.tm_vd);
-        tma_prefetch_desc(&p.tm_o);
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_holder;
+    constexpr uint32_t kBytes = Cfg::kTileBytes;
 
-    if (warp == 8) {
-        // ------------------------------------------------------------ TMA producer
-        if (lane == 0) {
-            constexpr uint32_t kBytes = Cfg::kTileBytes;
-            const int head0 = hk * p.G;
-            if (tA.len() > 0) {
-                mbar_expect_tx(q_full(0), kBytes);
-                for (int cb = 0; cb < Cfg::kColBlocks; ++cb)
-                    tma_load_4d(&p.tm_q, sQ + cb * 16384, q_full(0), cb * 64, head0, tA.t0, b);
-            }
-            if (tB.len() > 0) {
-                mbar_expect_tx(q_full(1), kBytes);
-                for (int cb = 0; cb < Cfg::kColBlocks; ++cb)
-                    tma_load_4d(&p.tm_q, sQ + kBytes + cb * 16384, q_full(1), cb * 64, head0,
-                                tB.t0, b);
-            }
-            uint32_t base = 0;
+    if (warp >= kWarpProducer) {
+        reg_dealloc<kProducerRegs>();
+        if (warp == kWarpProducer && lane == 0) {
+            // ------------------------------------------------------------ TMA producer
+            uint32_t f = 0;          // fills issued (ring position)
+            uint32_t quse[2] = {0, 0};
+            // per slot: which tiles read its current fill (2 bits), and the parity of
+            // the next release to wait for from each tile (1 bit per slot)
+            uint32_t cons = 0, par_a = 0, par_b = 0;
             bool ok = true;
-            auto fill = [&](uint32_t f, const CUtensorMap* map, int row0) {
-                const uint32_t slot = f % Cfg::kStages;
-                const uint32_t use = f / Cfg::kStages;
-                if (!mbar_wait(slot_empty(slot), (use & 1u) ^ 1u, abort_flag, 1)) return false;
-                mbar_expect_tx(slot_full(slot), kBytes);
-                const uint32_t dst = sRing + slot * kBytes;
-                for (int cb = 0; cb < Cfg::kColBlocks; ++cb)
-                    tma_load_4d(map, dst + cb * 16384, slot_full(slot), cb * 64, row0, hk, b);
-                return true;
-            };
-            auto k_src = [&](const TileInfo& ti, int s, int& row0) -> const CUtensorMap* {
-                if (is_depth(ti, s)) {
-                    row0 = ti.t0 * p.L + kBN * s;
-                    return &p.tm_kd;
+            for (int item = blockIdx.x; item < p.num_items && ok; item += gridDim.x) {
+                const Item it = item_info(p, item);
+#pragma unroll
+                for (int x = 0; x < 2; ++x) {
+                    if (!ok || it.t[x].len() == 0) continue;
+                    ok = mbar_wait(q_empty(x), (quse[x] & 1u) ^ 1u, abort_flag, 1);
+                    if (!ok) continue;
+                    mbar_expect_tx(q_full(x), kBytes);
+                    for (int cb = 0; cb < Cfg::kColBlocks; ++cb)
+                        tma_load_4d(&p.tm_q, sQ + x * kBytes + cb * 16384, q_full(x), cb * 64,
+                                    it.hk * p.G, it.t[x].t0, it.b);
+                    ++quse[x];
                 }
-                row0 = kBN * (s - ti.ndep);
-                return &p.tm_k;
-            };
-            auto v_src = [&](const TileInfo& ti, int s, int& row0) -> const CUtensorMap* {
-                if (is_depth(ti, s)) {
-                    row0 = ti.t0 * p.L + kBN * s;
-                    return &p.tm_vd;
+                StepWalker w(it);
+                for (int s = 0; s < it.nsteps() && ok; ++s) {
+                    const Step st = w.next(it);
+                    const Fills fl = step_fills(st, f);
+                    // fill order: K_A, K_B, V_A, V_B (a shared causal block is filled once)
+#pragma unroll
+                    for (int kv = 0; kv < 2; ++kv) {
+#pragma unroll
+                        for (int x = 0; x < 2; ++x) {
+                            if (!ok || !st.has[x] || (x == 1 && fl.shared)) continue;
+                            const uint32_t fi = kv == 0 ? fl.k[x] : fl.v[x];
+                            const uint32_t slot = fi % Cfg::kStages;
+                            // wait until every tile that read the slot's previous fill released it
+                            const uint32_t prev = (cons >> (2 * slot)) & 3u;
+                            if (prev & 1u) {
+                                ok = ok && mbar_wait(slot_empty(0, slot), (par_a >> slot) & 1u, abort_flag, 2);
+                                par_a ^= 1u << slot;
+                            }
+                            if (prev & 2u) {
+                                ok = ok && mbar_wait(slot_empty(1, slot), (par_b >> slot) & 1u, abort_flag, 2);
+                                par_b ^= 1u << slot;
+                            }
+                            if (!ok) continue;
+                            const uint32_t readers = fl.shared ? 3u : (1u << x);
+                            cons = (cons & ~(3u << (2 * slot))) | (readers << (2 * slot));
+                            const CUtensorMap* m;
+                            int row0;
+                            if (st.dep) {
+                                m = kv == 0 ? &p.tm_kd : &p.tm_vd;
+                                row0 = it.t[x].t0 * p.L + kBN * st.idx;
+                            } else {
+                                m = kv == 0 ? &p.tm_k : &p.tm_v;
+                                row0 = kBN * st.idx;
+                            }
+                            mbar_expect_tx(slot_full(slot), kBytes);
+                            for (int cb = 0; cb < Cfg::kColBlocks; ++cb)
+                                tma_load_4d(m, sRing + slot * kBytes + cb * 16384, slot_full(slot),
+                                            cb * 64, row0, it.hk, it.b);
+                            *issued = fi + 1;
+                        }
+                    }
+                    if (ok) f += fl.n;
                 }
-                row0 = kBN * (s - ti.ndep);
-                return &p.tm_v;
-            };
-            uint32_t issued = 0;  // fills whose TMA loads were started
-            for (int s = 0; s < nsteps && ok; ++s) {
-                const StepSlots st = step_slots(tA, tB, s, base);
-                int row0;
-                const CUtensorMap* m;
-                if (st.hasA) { m = k_src(tA, s, row0); ok = fill(st.kA, m, row0); issued += ok; }
-                if (ok && st.hasB && !st.shared) { m = k_src(tB, s, row0); ok = fill(st.kB, m, row0); issued += ok; }
-                if (ok && st.hasA) { m = v_src(tA, s, row0); ok = fill(st.vA, m, row0); issued += ok; }
-                if (ok && st.hasB && !st.shared) { m = v_src(tB, s, row0); ok = fill(st.vB, m, row0); issued += ok; }
-                base += st.nfill;
             }
-            // Exit path: the last loads of every slot must have landed before the
-            // CTA's shared memory is released (already true when all went well).
-            const uint32_t first = issued > Cfg::kStages ? issued - Cfg::kStages : 0;
-            for (uint32_t f = first; f < issued; ++f)
-                mbar_wait_drain(slot_full(f % Cfg::kStages), (f / Cfg::kStages) & 1u);
-            if (tA.len() > 0) mbar_wait_drain(q_full(0), 0);
-            if (tB.len() > 0) mbar_wait_drain(q_full(1), 0);
-        }
-    } else if (warp == 9) {
-        // ------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
+            // Exit path: loads still in flight must land before shared memory is released
+            // (a no-op when everything was consumed).
+            const uint32_t first = f > Cfg::kStages ? f - Cfg::kStages : 0;
+            for (uint32_t fi = first; fi < f; ++fi)
+                mbar_wait_drain(slot_full(fi % Cfg::kStages), (fi / Cfg::kStages) & 1u);
+            for (int x = 0; x < 2; ++x)
+                if (quse[x] > 0) mbar_wait_drain(q_full(x), (quse[x] - 1) & 1u);
+        } else if ((warp == kWarpMmaA || warp == kWarpMmaB) && lane == 0) {
+            // ------------------------------------------------------------ MMA issuer (tile x)
+            const int x = warp - kWarpMmaA;
             constexpr uint32_t idesc_s = make_idesc(FMT, kBM, kBN, 0);
             constexpr uint32_t idesc_pv = make_idesc(FMT, kBM, HD, 1);
-            constexpr uint32_t kBytes = Cfg::kTileBytes;
-            bool ok = true;
-            // Q tiles are needed by the first S MMA of each tile.
-            if (tA.len() > 0) ok = ok && mbar_wait(q_full(0), 0, abort_flag, 2);
-            if (ok && tB.len() > 0) ok = mbar_wait(q_full(1), 0, abort_flag, 2);
+            // Descriptors are built once; each MMA advances the start address with a
+            // single 32-bit add (K-major Q/K: 32 B per 16-wide k step inside a 128-byte
+            // swizzle atom, 16 KB per atom; V MN-major: 2 KB per 16 key rows).
+            constexpr uint32_t hi = desc_hi_sw128(1024);
+            const uint32_t qa = desc_lo(sQ + x * kBytes, 16);
+            const uint32_t ring_lo_k = desc_lo(sRing, 16);
+            const uint32_t ring_lo_v = desc_lo(sRing, 128 * 128);
+            constexpr uint32_t kSlotStep = kBytes >> 4;  // descriptor units per ring slot
+            const uint32_t s_tm = tmem + x * 128;
+            const uint32_t p_tm = s_tm + 64;
+            const uint32_t o_tm = tmem + Cfg::kOCol + x * HD;
+            const uint32_t rel_bar0 = slot_empty(x, 0);
 
-            auto issue_s = [&](int x, uint32_t f) {
-                const uint32_t slot = f % Cfg::kStages;
-                if (!mbar_wait(slot_full(slot), (f / Cfg::kStages) & 1u, abort_flag, 3)) return false;
-                tc_fence_after();
-                const uint32_t qa = sQ + x * kBytes;
-                const uint32_t kb = sRing + slot * kBytes;
+            auto wait_issued = [&](uint32_t fi) {
+                if (*issued > fi) return true;
+                const long long t0 = clock64();
+                for (uint32_t i = 1;; ++i) {
+                    if (*issued > fi) return true;
+                    if ((i & 255u) == 0) {
+                        if (*abort_flag) return false;
+                        if (clock64() - t0 > kWaitLimitCycles) {
+                            *abort_flag = 1;
+                            atomicCAS(&moda_dev_status, 0, 0x100 | 11);
+                            return false;
+                        }
+                    }
+                }
+            };
+            auto wait_full = [&](uint32_t fi) {
+                return wait_issued(fi) &&
+                       mbar_wait(slot_full(fi % Cfg::kStages), (fi / Cfg::kStages) & 1u, abort_flag, 3);
+            };
+            auto issue_s = [&](uint32_t fi) {
+                const uint32_t kb = ring_lo_k + (fi % Cfg::kStages) * kSlotStep;
 #pragma unroll
                 for (int kk = 0; kk < HD / 16; ++kk) {
-                    const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-                    mma_ss(tmem + x * 128, smem_desc_sw128(qa + off, 16, 1024),
-                           smem_desc_sw128(kb + off, 16, 1024), idesc_s, kk > 0);
+                    const uint32_t off = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
+                    mma_ss(s_tm, desc_join(qa + off, hi), desc_join(kb + off, hi), idesc_s, kk > 0);
                 }
                 mma_commit(s_full(x));
-                return true;
+                mma_commit(rel_bar0 + 8u * (fi % Cfg::kStages));
             };
-            auto issue_pv = [&](int x, uint32_t f, bool first) {
-                const uint32_t slot = f % Cfg::kStages;
-                if (!mbar_wait(slot_full(slot), (f / Cfg::kStages) & 1u, abort_flag, 4)) return false;
-                tc_fence_after();
-                const uint32_t vb = sRing + slot * kBytes;
-                const uint32_t ptm = tmem + x * 128 + 64;
-                const uint32_t otm = tmem + Cfg::kOCol + x * HD;
+            auto issue_pv = [&](uint32_t fi, bool first) {
+                const uint32_t vb = ring_lo_v + (fi % Cfg::kStages) * kSlotStep;
+                mma_ts(o_tm, p_tm, desc_join(vb, hi), idesc_pv, first ? 0u : 1u);
 #pragma unroll
-                for (int kk = 0; kk < kBN / 16; ++kk) {
-                    mma_ts(otm, ptm + kk * 8, smem_desc_sw128(vb + kk * 2048, 128 * 128, 1024),
-                           idesc_pv, (first && kk == 0) ? 0u : 1u);
-                }
-                mma_commit(o_done(x));
-                return true;
+                for (int kk = 1; kk < kBN / 16; ++kk)
+                    mma_ts(o_tm, p_tm + kk * 8, desc_join(vb + ((kk * 2048) >> 4), hi), idesc_pv, 1u);
+                mma_commit(rel_bar0 + 8u * (fi % Cfg::kStages));
             };
 
-            StepSlots cur = step_slots(tA, tB, 0, 0);
-            uint32_t base_next = cur.nfill;
-            // prologue: S of step 0 for both tiles
-            if (ok && cur.hasA) {
-                ok = issue_s(0, cur.kA);
-                if (ok && !cur.shared) mma_commit(slot_empty(cur.kA % Cfg::kStages));
-            }
-            if (ok && cur.hasB) {
-                ok = issue_s(1, cur.kB);
-                if (ok) mma_commit(slot_empty(cur.kB % Cfg::kStages));
-            }
-            for (int s = 0; s < nsteps && ok; ++s) {
-                const StepSlots nxt = step_slots(tA, tB, s + 1, base_next);
-                if (cur.hasA) {
-                    ok = mbar_wait(p_full(0), s & 1, abort_flag, 5);
+            uint32_t f = 0;       // ring position (same fill sequence as the producer)
+            uint32_t pcnt = 0;    // P blocks consumed
+            uint32_t items = 0;   // items of this tile started
+            bool ok = true;
+            for (int item = blockIdx.x; item < p.num_items && ok; item += gridDim.x) {
+                const Item it = item_info(p, item);
+                const TileInfo ti = x == 0 ? it.t[0] : it.t[1];
+                if (ti.len() == 0) {
+                    // still walk the fills so the ring position stays in step with the producer
+                    StepWalker w(it);
+                    for (int s = 0; s < it.nsteps(); ++s) f += step_fills(w.next(it), f).n;
+                    continue;
+                }
+                // Blocks of this tile in step order; the walker runs one block ahead.
+                StepWalker w(it);
+                uint32_t fcur = f;
+                Step st;
+                Fills fl;
+                // advance to this tile's first block
+                do {
+                    st = w.next(it);
+                    fl = step_fills(st, fcur);
+                    if (!(x == 0 ? st.has[0] : st.has[1])) fcur += fl.n;
+                } while (!(x == 0 ? st.has[0] : st.has[1]));
+                int steps_left = it.nsteps() - (w.j + w.k);
+                uint32_t kf = x == 0 ? fl.k[0] : fl.k[1];
+                uint32_t vf = x == 0 ? fl.v[0] : fl.v[1];
+                ok = mbar_wait(q_full(x), items & 1u, abort_flag, 5) && wait_full(kf);
+                if (!ok) break;
+                tc_fence_after();
+                issue_s(kf);
+                fcur += fl.n;
+                for (int b = 0; b < ti.len() && ok; ++b) {
+                    // find the next block of this tile (if any) and its fills
+                    bool has_next = false;
+                    uint32_t kf_next = 0, vf_next = 0;
+                    while (steps_left > 0) {
+                        const Step sn = w.next(it);
+                        const Fills fn = step_fills(sn, fcur);
+                        --steps_left;
+                        fcur += fn.n;
+                        if (x == 0 ? sn.has[0] : sn.has[1]) {
+                            has_next = true;
+                            kf_next = x == 0 ? fn.k[0] : fn.k[1];
+                            vf_next = x == 0 ? fn.v[0] : fn.v[1];
+                            break;
+                        }
+                    }
+                    // This block's V slot first (normally loaded long ago), then the softmax's
+                    // P. The next K slot is only probed here: blocking on it before the PV
+                    // below releases this block's V slot could deadlock the ring when the
+                    // next block is more than a ring's length of fills ahead.
+                    ok = wait_full(vf);
+                    const bool k_ready = ok && has_next && *issued > kf_next &&
+                                         mbar_test(slot_full(kf_next % Cfg::kStages),
+                                                   (kf_next / Cfg::kStages) & 1u);
+                    ok = ok && mbar_wait(p_full(x), pcnt & 1u, abort_flag, 6);
                     if (!ok) break;
-                    tc_fence_after();
-                    ok = issue_pv(0, cur.vA, s == 0);
-                    if (!ok) break;
-                    if (!cur.shared) mma_commit(slot_empty(cur.vA % Cfg::kStages));
-                    if (nxt.hasA) {
-                        ok = issue_s(0, nxt.kA);
+                    ++pcnt;
+                    if (b == 0 && items > 0) {
+                        // the epilogue of this tile's previous item must have read O
+                        ok = mbar_wait(o_free(x), (items - 1) & 1u, abort_flag, 7);
                         if (!ok) break;
-                        if (!nxt.shared) mma_commit(slot_empty(nxt.kA % Cfg::kStages));
+                    }
+                    tc_fence_after();
+                    issue_pv(vf, b == 0);
+                    if (has_next) {
+                        if (!k_ready) {
+                            ok = wait_full(kf_next);
+                            if (!ok) break;
+                            tc_fence_after();
+                        }
+                        issue_s(kf_next);
+                        vf = vf_next;
+                    } else {
+                        mma_commit(o_done(x));   // the item's last PV: epilogue may read O
+                        mma_commit(q_empty(x));  // and every S of the item is complete
                     }
                 }
-                if (cur.hasB) {
-                    ok = mbar_wait(p_full(1), s & 1, abort_flag, 6);
-                    if (!ok) break;
-                    tc_fence_after();
-                    ok = issue_pv(1, cur.vB, s == 0);
-                    if (!ok) break;
-                    mma_commit(slot_empty(cur.vB % Cfg::kStages));
-                    if (nxt.hasB) {
-                        ok = issue_s(1, nxt.kB);
-                        if (!ok) break;
-                        mma_commit(slot_empty(nxt.kB % Cfg::kStages));
-                    }
+                // walk the remaining steps of the item (fills of the other tile only)
+                while (steps_left > 0) {
+                    fcur += step_fills(w.next(it), fcur).n;
+                    --steps_left;
                 }
-                cur = nxt;
-                base_next += nxt.nfill;
+                f = fcur;
+                ++items;
             }
             // every MMA issued above has completed once end_bar flips
-            mma_commit(end_bar);
-            mbar_wait_drain(end_bar, 0);
+            mma_commit(end_bar(x));
+            mbar_wait_drain(end_bar(x), 0);
         }
     } else {
+        reg_alloc<kSoftmaxRegs>();
         // ------------------------------------------------------------ softmax warpgroups
-        const int x = warp >> 2;  // tile
-        const TileInfo ti = x == 0 ? tA : tB;
-        const int row = threadIdx.x & 127;
-        const int wq = warp & 3;  // TMEM lane quarter of this warp
+        const int x = warp >> 3;        // tile
+        const int half = (warp >> 2) & 1;  // score columns [64*half, 64*half + 64)
+        const int wq = warp & 3;        // TMEM lane quarter of this warp
+        const int row = wq * 32 + lane;
         const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
-        const uint32_t tS = tmem + lane_off + x * 128;
-        const uint32_t tP = tS + 64;
-        const uint32_t tO = tmem + lane_off + Cfg::kOCol + x * HD;
-        const int tok = ti.t0 + row / p.G;
+        const uint32_t tS = tmem + lane_off + x * 128 + 64 * half;
+        const uint32_t tP = tmem + lane_off + x * 128 + 64 + 32 * half;
+        constexpr int kHalfD = HD / 2;
+        const uint32_t tO = tmem + lane_off + Cfg::kOCol + x * HD + kHalfD * half;
+        const int pair_bar = 1 + x * 4 + wq;  // named barrier of the two warps of this quarter
+        float* xmax = reinterpret_cast<float*>(smem + Cfg::kXmaxOff) + x * 512;  // [parity][half][row]
+        float* xsum = reinterpret_cast<float*>(smem + Cfg::kXsumOff) + x * 256;  // [half][row]
         const float sc = p.sc;
-        float m_run = -INFINITY, l_run = 0.f;
+        uint32_t nblk = 0;   // blocks processed by this tile slot (s_full / p_full phase)
+        uint32_t nitem = 0;  // items finished by this tile slot (o_done / o_free phase)
+        uint32_t other_before = 0;  // blocks of the other tile in earlier items
+        volatile uint32_t* other_turns = exp_turns + (x ^ 1);
         bool ok = true;
-        const int len = ti.len();
-        for (int s = 0; s < len; ++s) {
-            if (!mbar_wait(s_full(x), s & 1, abort_flag, 8)) { ok = false; break; }
-            tc_fence_after();
-            uint32_t sv[128];
-            {
-                uint32_t (&c0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sv[0]);
-                uint32_t (&c1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sv[32]);
-                uint32_t (&c2)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sv[64]);
-                uint32_t (&c3)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sv[96]);
-                tmem_ld32(tS + 0, c0);
-                tmem_ld32(tS + 32, c1);
-                tmem_ld32(tS + 64, c2);
-                tmem_ld32(tS + 96, c3);
-                tmem_wait_ld();
+        for (int item = blockIdx.x; item < p.num_items && ok; item += gridDim.x) {
+            const Item it = item_info(p, item);
+            const TileInfo ti = x == 0 ? it.t[0] : it.t[1];
+            const int other_len = x == 0 ? it.t[1].len() : it.t[0].len();
+            if (ti.len() == 0) {
+                other_before += other_len;
+                continue;
             }
-            // mask: keep columns c with lo <= c < hi
-            int lo = 0, hi = kBN;
-            bool need_mask;
-            if (is_depth(ti, s)) {
-                lo = (tok - ti.t0) * p.L - kBN * s;
-                hi = lo + p.L;
-                need_mask = true;
-            } else {
-                const int j0 = kBN * (s - ti.ndep);
-                hi = tok - j0 + 1;
-                need_mask = (j0 + kBN - 1) > ti.t0;
-            }
-            float mx = -INFINITY;
-            if (need_mask) {
-#pragma unroll
-                for (int c = 0; c < 128; ++c) {
-                    const bool keep = (c >= lo) && (c < hi);
-                    float v = keep ? __uint_as_float(sv[c]) : -INFINITY;
-                    sv[c] = __float_as_uint(v);
-                    mx = fmaxf(mx, v);
-                }
-            } else {
-#pragma unroll
-                for (int c = 0; c < 128; ++c) mx = fmaxf(mx, __uint_as_float(sv[c]));
-            }
-            const float m_blk = mx * sc;
-            const float m_new = fmaxf(m_run, m_blk);
-            // lazy rescale: keep the stale max unless it grew by more than 2^8
-            const bool rescale = m_new > m_run + 8.0f;
-            const float m_use = rescale ? m_new : m_run;
-            const float alpha = rescale ? ex2(m_run - m_use) : 1.0f;
-            const float m_base = (m_use == -INFINITY) ? 0.f : m_use;
-            float sum = 0.f;
-            uint32_t pk[64];
-#pragma unroll
-            for (int c = 0; c < 128; c += 2) {
-                const float p0 = ex2(fmaf(__uint_as_float(sv[c]), sc, -m_base));
-                const float p1 = ex2(fmaf(__uint_as_float(sv[c + 1]), sc, -m_base));
-                sum += p0 + p1;
-                pk[c >> 1] = FMT == 1 ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
-            }
-            l_run = fmaf(l_run, alpha, sum);
-            m_run = m_use;
-            tmem_st32(tP, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
-            tmem_st32(tP + 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
-            if (s > 0 && __any_sync(0xffffffffu, rescale)) {
-                if (!mbar_wait(o_done(x), (s - 1) & 1, abort_flag, 9)) { ok = false; break; }
+            uint32_t other_seen = other_before;  // other-tile blocks at earlier steps of this item
+            const int tok = ti.t0 + row / p.G;
+            float m_run = -INFINITY, l_run = 0.f;  // l_run: this half's share of the row sum
+            StepWalker w(it);
+            int done = 0;
+            for (int s = 0; s < it.nsteps(); ++s) {
+                const Step st = w.next(it);
+                const bool mine = x == 0 ? st.has[0] : st.has[1];
+                const bool theirs = x == 0 ? st.has[1] : st.has[0];
+                // tile A goes first within a step, tile B follows A's block of the same step
+                if (x == 1 && theirs) ++other_seen;
+                const uint32_t turn_target = other_seen;
+                if (x == 0 && theirs) ++other_seen;
+                if (!mine) continue;
+                if (!mbar_wait(s_full(x), nblk & 1u, abort_flag, 8)) { ok = false; break; }
                 tc_fence_after();
-#pragma unroll
-                for (int cb = 0; cb < HD; cb += 32) {
-                    uint32_t ov[32];
-                    tmem_ld32(tO + cb, ov);
+                uint32_t sv[64];
+                {
+                    uint32_t r0[32], r1[32];
+                    tmem_ld32(tS, r0);
+                    tmem_ld32(tS + 32, r1);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
-                    tmem_st32(tO + cb, ov);
+                    for (int i = 0; i < 32; ++i) {
+                        sv[i] = r0[i];
+                        sv[32 + i] = r1[i];
+                    }
                 }
-            }
-            tmem_wait_st();
-            tc_fence_before();
-            mbar_arrive(p_full(x));
-        }
-        // ------------------------------------------------------------ epilogue
-        // Runs whenever the tile has work, even after an abort (then the output is
-        // garbage and the host sees the status word): the named barrier below
-        // needs all four warps of the warpgroup.
-        if (len > 0) {
-            if (ok) mbar_wait(o_done(x), (len - 1) & 1, abort_flag, 10);
-            tc_fence_after();
-            const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-            const uint32_t tile = sQ + x * Cfg::kTileBytes;  // Q tile is free: reuse as staging
+                // keep columns c (of the 128-wide block) with lo <= c < hi
+                int lo = 0, hi = kBN;
+                bool need_mask;
+                if (st.dep) {
+                    lo = (tok - ti.t0) * p.L - kBN * st.idx;
+                    hi = lo + p.L;
+                    need_mask = true;
+                } else {
+                    const int j0 = kBN * st.idx;
+                    hi = tok - j0 + 1;
+                    need_mask = (j0 + kBN - 1) > ti.t0;
+                }
+                lo -= 64 * half;  // into this warp's column range
+                hi -= 64 * half;
+                const bool live = !need_mask || (lo < hi && hi > 0 && lo < 64);
+                float mx = -INFINITY;
+                if (__any_sync(0xffffffffu, live)) {
+                    if (need_mask) {
 #pragma unroll
-            for (int cb = 0; cb < HD; cb += 32) {
+                        for (int c = 0; c < 64; ++c) {
+                            const bool keep = (c >= lo) && (c < hi);
+                            sv[c] = keep ? sv[c] : __float_as_uint(-INFINITY);
+                        }
+                    }
+                    float mx4[4];
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        float a = __uint_as_float(sv[16 * k]);
+#pragma unroll
+                        for (int i = 1; i < 15; i += 2)
+                            a = fmax3(a, __uint_as_float(sv[16 * k + i]), __uint_as_float(sv[16 * k + i + 1]));
+                        mx4[k] = fmaxf(a, __uint_as_float(sv[16 * k + 15]));
+                    }
+                    mx = fmaxf(fmax3(mx4[0], mx4[1], mx4[2]), mx4[3]);
+                }
+                // trade partial row maxima with the partner warp (double-buffered by block parity)
+                float* xm = xmax + (nblk & 1u) * 256;
+                xm[half * 128 + row] = mx;
+                named_bar_sync(pair_bar, 64);
+                mx = fmaxf(mx, xm[(half ^ 1) * 128 + row]);
+                const float m_new = fmaxf(m_run, mx * sc);
+                // lazy rescale: keep the stale max unless it grew by more than 2^8
+                const bool rescale = m_new > m_run + 8.0f;
+                const float m_use = rescale ? m_new : m_run;
+                const float alpha = rescale ? ex2(m_run - m_use) : 1.0f;
+                m_run = m_use;
+                // wait for the other tile's turn to end (bounded; skipped after an abort)
+                if (lane == 0) {
+                    const uint32_t need = 8u * turn_target;
+                    const long long t0 = clock64();
+                    while (*other_turns < need && !*abort_flag) {
+                        if (clock64() - t0 > kWaitLimitCycles / 64) break;  // hint only: never stall long
+                    }
+                }
+                __syncwarp();
+                if (__any_sync(0xffffffffu, live)) {
+                    const float m_base = (m_use == -INFINITY) ? 0.f : m_use;
+                    const uint64_t sc2 = f2_pack(sc, sc);
+                    const uint64_t nm2 = f2_pack(-m_base, -m_base);
+                    uint64_t acc[4];
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) acc[k] = 0ull;
+#pragma unroll
+                    for (int q4 = 0; q4 < 2; ++q4) {
+                        uint32_t pk[16];
+#pragma unroll
+                        for (int c = 0; c < 32; c += 2) {
+                            const int cc = 32 * q4 + c;
+                            const uint64_t xx = f2_fma(
+                                f2_pack(__uint_as_float(sv[cc]), __uint_as_float(sv[cc + 1])), sc2, nm2);
+                            float x0, x1;
+                            f2_unpack(xx, x0, x1);
+                            const float p0 = ex2(x0), p1 = ex2(x1);
+                            acc[(c >> 1) & 3] = f2_add(acc[(c >> 1) & 3], f2_pack(p0, p1));
+                            pk[c >> 1] = FMT == 1 ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
+                        }
+                        tmem_st16(tP + 16 * q4, pk);
+                    }
+                    float s0, s1;
+                    f2_unpack(f2_add(f2_add(acc[0], acc[1]), f2_add(acc[2], acc[3])), s0, s1);
+                    l_run = fmaf(l_run, alpha, s0 + s1);
+                } else {
+                    uint32_t z[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) z[i] = 0u;
+                    tmem_st16(tP, z);
+                    tmem_st16(tP + 16, z);
+                    l_run *= alpha;
+                }
+                __syncwarp();
+                if (lane == 0) atomicAdd(exp_turns + x, 1u);  // this warp's exponentials are done
+                if (done > 0 && __any_sync(0xffffffffu, rescale)) {
+                    // This half's O columns hold the previous blocks' sum. Their PV has
+                    // completed: the S just read was issued after it by the same thread,
+                    // and its commit covers both.
+                    const uint64_t al2 = f2_pack(alpha, alpha);
+#pragma unroll
+                    for (int cb = 0; cb < kHalfD; cb += 32) {
+                        uint32_t ov[32];
+                        tmem_ld32(tO + cb, ov);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 32; i += 2) {
+                            float a, c;
+                            f2_unpack(f2_mul(f2_pack(__uint_as_float(ov[i]), __uint_as_float(ov[i + 1])), al2), a, c);
+                            ov[i] = __float_as_uint(a);
+                            ov[i + 1] = __float_as_uint(c);
+                        }
+                        tmem_st32(tO + cb, ov);
+                    }
+                }
+                tmem_wait_st();
+                tc_fence_before();
+                mbar_arrive(p_full(x));
+                ++nblk;
+                ++done;
+            }
+            other_before += other_len;
+            if (!ok) break;
+            // ------------------------------------------------------------ epilogue
+            // O = sum / l for this half's columns, straight from TMEM to global memory.
+            if (!mbar_wait(o_done(x), nitem & 1u, abort_flag, 10)) { ok = false; break; }
+            ++nitem;
+            tc_fence_after();
+            xsum[half * 128 + row] = l_run;
+            named_bar_sync(pair_bar, 64);
+            const float l_tot = l_run + xsum[(half ^ 1) * 128 + row];
+            named_bar_sync(pair_bar, 64);  // both read before the next item overwrites
+            const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
+            const bool valid = tok < ti.tend;
+            const int head = it.hk * p.G + row % p.G;
+            uint4* dst = reinterpret_cast<uint4*>(
+                static_cast<uint16_t*>(p.o) + it.b * p.o_sb + head * p.o_sh +
+                static_cast<long long>(tok) * p.o_st + kHalfD * half);
+#pragma unroll
+            for (int cb = 0; cb < kHalfD; cb += 32) {
                 uint32_t ov[32];
                 tmem_ld32(tO + cb, ov);
                 tmem_wait_ld();
@@ -431,31 +666,20 @@ __global__ void __launch_bounds__(kThreads, 1) moda_fwd_tc_kernel(const __grid_c
                     const float c = __uint_as_float(ov[2 * i + 1]) * inv;
                     pk[i] = FMT == 1 ? pack_bf16x2(a, c) : pack_f16x2(a, c);
                 }
-                const int colblk = cb >> 6;
+                if (valid) {
 #pragma unroll
-                for (int ch = 0; ch < 4; ++ch) {
-                    const int chunk = ((cb & 63) >> 3) + ch;  // 16-byte chunk within the 128-byte row
-                    const uint32_t addr = tile + colblk * 16384 + row * 128 + ((chunk ^ (row & 7)) << 4);
-                    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr),
-                                 "r"(pk[4 * ch]), "r"(pk[4 * ch + 1]), "r"(pk[4 * ch + 2]),
-                                 "r"(pk[4 * ch + 3])
-                                 : "memory");
+                    for (int ch = 0; ch < 4; ++ch)
+                        dst[(cb >> 3) + ch] = make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
                 }
             }
-            fence_proxy_async_smem();
-            named_bar_sync(1 + x, 128);
-            if (row == 0) {
-                for (int cb = 0; cb < Cfg::kColBlocks; ++cb)
-                    tma_store_4d(&p.tm_o, tile + cb * 16384, cb * 64, hk * p.G, ti.t0, b);
-                bulk_commit();
-                bulk_wait0();
-            }
+            tc_fence_before();
+            mbar_arrive(o_free(x));
         }
     }
 
     tc_fence_before();
     __syncthreads();
-    if (warp == 9) {
+    if (warp == kWarpMmaA) {
         tc_fence_after();
         tmem_dealloc(tmem, Cfg::kTmemCols);
     }
@@ -569,6 +793,11 @@ static int launch_tc_inst(const TcParams& tp, int grid, cudaStream_t stream) {
     auto kern = moda_fwd_tc_kernel<HD, FMT>;
     static bool attr_set = false;
     if (!attr_set) {
+        // The setmaxnreg split assumes exactly kLaunchRegs registers per thread at
+        // launch; with fewer, the softmax warpgroups' increase could never be granted.
+        cudaFuncAttributes fa;
+        if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess || fa.numRegs != kLaunchRegs)
+            return MODA_ERR_UNSUPPORTED;
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  Cfg::kSmemBytes) != cudaSuccess)
             return MODA_ERR_LAUNCH;
@@ -578,6 +807,14 @@ static int launch_tc_inst(const TcParams& tp, int grid, cudaStream_t stream) {
     return MODA_OK;
 }
 
+static int sm_count() {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+        return 148;
+    return n;
+}
+
 int launch_fwd_tc(const FwdParams& p, cudaStream_t stream, char* err, size_t errlen) {
     TcParams tp;
     const CUtensorMapDataType dt =
@@ -585,7 +822,6 @@ int launch_fwd_tc(const FwdParams& p, cudaStream_t stream, char* err, size_t err
     const int n_tok = 128 / p.G;
     const int rows_depth = p.T * p.L;
     if (!encode_map(&tp.tm_q, p.q, p.T, true, 2, dt, p.G, n_tok, err, errlen, "Q") ||
-        !encode_map(&tp.tm_o, p.o, p.T, true, 2, dt, p.G, n_tok, err, errlen, "O") ||
         !encode_map(&tp.tm_k, p.k, p.T, false, 2, dt, kBN, 1, err, errlen, "K") ||
         !encode_map(&tp.tm_v, p.v, p.T, false, 2, dt, kBN, 1, err, errlen, "V") ||
         !encode_map(&tp.tm_kd, rows_depth > 0 ? p.kd : p.k, rows_depth > 0 ? rows_depth : p.T,
@@ -593,6 +829,10 @@ int launch_fwd_tc(const FwdParams& p, cudaStream_t stream, char* err, size_t err
         !encode_map(&tp.tm_vd, rows_depth > 0 ? p.vd : p.v, rows_depth > 0 ? rows_depth : p.T,
                     false, 2, dt, kBN, 1, err, errlen, "V_depth"))
         return MODA_ERR_LAUNCH;  // with L == 0 the depth maps are placeholders, never loaded
+    tp.o = p.o.ptr;
+    tp.o_sb = p.o.strides[0];
+    tp.o_sh = p.o.strides[1];
+    tp.o_st = p.o.strides[2];
     tp.B = p.B;
     tp.Hq = p.Hq;
     tp.Hk = p.Hk;
@@ -602,13 +842,14 @@ int launch_fwd_tc(const FwdParams& p, cudaStream_t stream, char* err, size_t err
     tp.n_tok = n_tok;
     tp.num_pairs = (p.T + 2 * n_tok - 1) / (2 * n_tok);
     tp.sc = p.scale * kLog2e;
-    const long long grid = static_cast<long long>(tp.num_pairs) * p.B * p.Hk;
-    if (grid == 0) return MODA_OK;
-    if (grid > 0x7fffffffLL) {
-        snprintf(err, errlen, "grid too large");
+    const long long items = static_cast<long long>(tp.num_pairs) * p.B * p.Hk;
+    if (items == 0) return MODA_OK;
+    if (items > 0x7fffffffLL) {
+        snprintf(err, errlen, "too many work items");
         return MODA_ERR_UNSUPPORTED;
     }
-    const int g = static_cast<int>(grid);
+    tp.num_items = static_cast<int>(items);
+    const int g = static_cast<int>(items < sm_count() ? items : sm_count());
     if (p.d == 128) return p.dtype == MODA_BF16 ? launch_tc_inst<128, 1>(tp, g, stream)
                                                 : launch_tc_inst<128, 0>(tp, g, stream);
     return p.dtype == MODA_BF16 ? launch_tc_inst<64, 1>(tp, g, stream)

@@ -22,10 +22,13 @@ struct AppendParams {
 
 // Parameters of the tcgen05 kernel. Tensor maps first (64-byte aligned).
 struct TcParams {
-    CUtensorMap tm_q, tm_k, tm_v, tm_kd, tm_vd, tm_o;
+    CUtensorMap tm_q, tm_k, tm_v, tm_kd, tm_vd;
+    void* o;                      // output [B, H_q, T, d], unit stride along d
+    long long o_sb, o_sh, o_st;   // output strides in elements
     int B, Hq, Hk, G, T, L;
     int n_tok;      // tokens per 128-row query tile (128 / G)
     int num_pairs;  // tile pairs per (b, kv head)
+    int num_items;  // num_pairs * B * Hk work items
     float sc;       // scale * log2(e)
 };
 
