@@ -217,10 +217,16 @@ def main():
     import torch.distributed as dist
     from moda.kernels import moda_attention_cuda, device_status
     from moda.kernels.moda_cuda import moda_forward_into
+    from moda.sharding import gather_checksums, output_checksum, shard_batches
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    # Libraries (NCCL) may print to the process's stdout; keep stdout for the one JSON
+    # line by pointing file descriptor 1 at stderr until that line is written.
+    sys.stdout.flush()
+    stdout_fd = os.dup(1)
+    os.dup2(2, 1)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
@@ -228,14 +234,9 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
 
     # shard: weak scaling gives every rank its own 4-batch; strong scaling splits 16 batches
-    if args.workload != "scaling":
-        b_lo, b_hi = rank * wl["B"], (rank + 1) * wl["B"]
-        B_global = wl["B"] * world
-    else:
-        per = wl["B"] // world
-        b_lo, b_hi = rank * per, (rank + 1) * per
-        B_global = wl["B"]
-    B = b_hi - b_lo
+    shard = shard_batches(wl["B"], world, rank, weak=args.workload != "scaling")
+    b_lo, b_hi, B_global = shard.b_lo, shard.b_hi, shard.global_batch
+    B = shard.batch
     Hq, Hk, T, d, L, C = wl["Hq"], wl["Hk"], wl["T"], wl["d"], wl["L"], wl["chunk"]
     dtype = torch.bfloat16
     Q, K, V, Kd, Vd = make_inputs(wl, b_lo, b_hi, dev, dtype)
@@ -284,13 +285,7 @@ def main():
     t_roof = max(f_rank / (p_tflops * 1e12), by_rank / (p_gbs * 1e9))
 
     # verification gather (NCCL, outside the timed region): per-rank output checksums
-    cs = torch.stack([O.float().sum(), O.float().abs().sum(),
-                      torch.isfinite(O).all().float()]).to(torch.float64)
-    if world > 1:
-        gathered = [torch.zeros_like(cs) for _ in range(world)]
-        dist.all_gather(gathered, cs)
-    else:
-        gathered = [cs]
+    gathered = gather_checksums(output_checksum(O))
     finite_all = all(bool(g[2].item() == 1.0) for g in gathered)
     status = device_status(dev)
 
@@ -338,6 +333,9 @@ def main():
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    sys.stdout.flush()
+    os.dup2(stdout_fd, 1)
+    os.close(stdout_fd)
     if rank != 0:
         return
     traffic = ncu_traffic_bytes(args.workload)
