@@ -1,5 +1,6 @@
 /*
- * moda_b200.h - C ABI of the B200 (sm_100a) fused MoDA forward library.
+ * moda_b200.h - C ABI of the B200 (sm_100a) fused MoDA attention library
+ * (forward, backward, depth-cache append).
  *
  * Plain pointers and sizes only: no PyTorch types cross this boundary. The
  * caller owns every buffer; the library never allocates device memory on the
@@ -68,6 +69,39 @@ int moda_fwd(const ModaTensor* q, const ModaTensor* k, const ModaTensor* v, cons
 int moda_fwd_ex(const ModaTensor* q, const ModaTensor* k, const ModaTensor* v,
                 const ModaTensor* kd, const ModaTensor* vd, const ModaTensor* o, int num_layers,
                 float scale, int chunk_size, int dtype, int kernel, moda_stream_t stream);
+
+/* moda_fwd_ex that also writes the row log-sum-exp the backward pass needs:
+ * lse[(b*H_q + h)*T + t] = log(sum over the row's keys of exp(scale*q.k)), natural log,
+ * float32, contiguous [B, H_q, T]. Same result O as moda_fwd_ex.
+ * Reference counterpart: the forward half of autograd through moda_attention_naive
+ * (moda/kernels/moda_naive.py:13-97), which keeps the softmax for its backward. */
+int moda_fwd_lse(const ModaTensor* q, const ModaTensor* k, const ModaTensor* v,
+                 const ModaTensor* kd, const ModaTensor* vd, const ModaTensor* o, float* lse,
+                 int num_layers, float scale, int chunk_size, int dtype, int kernel,
+                 moda_stream_t stream);
+
+/* Bytes of device workspace moda_bwd needs (one float per query row), or -1 for
+ * negative sizes. No reference counterpart. */
+int64_t moda_bwd_workspace_size(int64_t batch, int64_t num_q_heads, int64_t seq_len);
+
+/*
+ * Backward of moda_fwd: given dout = dL/dO and the forward's o and lse, writes
+ *   dq [B,H_q,T,d], dk, dv [B,H_k,T,d], dkd, dvd [B,H_k,R,d]
+ * in full (each shaped like its input; depth rows at or beyond T*num_layers, which
+ * the forward never reads, get zero). GQA gradients are summed over the G query
+ * heads of each KV head. workspace: device memory of at least
+ * moda_bwd_workspace_size(B, H_q, T) bytes, used for rowsum(dO*O); nothing is
+ * allocated. Any strides; fp32 arithmetic.
+ * Replaces torch autograd through moda_attention_naive (moda/kernels/moda_naive.py:
+ * 13-162), which the reference trains with (tests/test_kernel.py:106-119,
+ * tests/test_attention.py:57-71).
+ */
+int moda_bwd(const ModaTensor* q, const ModaTensor* k, const ModaTensor* v, const ModaTensor* kd,
+             const ModaTensor* vd, const ModaTensor* o, const ModaTensor* dout, const float* lse,
+             const ModaTensor* dq, const ModaTensor* dk, const ModaTensor* dv,
+             const ModaTensor* dkd, const ModaTensor* dvd, void* workspace,
+             int64_t workspace_bytes, int num_layers, float scale, int dtype,
+             moda_stream_t stream);
 
 /* Which kernel moda_fwd_ex would launch for these arguments (ModaKernel value,
  * or a negative ModaStatus). Host-only: validates and plans, launches nothing.

@@ -97,6 +97,7 @@ int validate_fwd(const ModaTensor* q, const ModaTensor* k, const ModaTensor* v,
     out->d = static_cast<int>(d);
     out->L = num_layers;
     out->scale = scale > 0.f ? scale : 1.0f / sqrtf(static_cast<float>(d));
+    out->lse = nullptr;
     out->dtype = dtype;
     return MODA_OK;
 }
@@ -115,6 +116,25 @@ int plan_kernel(const moda::FwdParams& p, int kernel) {
     }
 }
 
+int launch_validated(const moda::FwdParams& p, int kernel, cudaStream_t st) {
+    const int which = plan_kernel(p, kernel);
+    if (which < 0) return which;
+    if (static_cast<int64_t>(p.B) * p.Hq * p.T * p.d == 0) return MODA_OK;  // nothing to write
+    cudaGetLastError();  // clear a stale error so the check below is ours
+    int r;
+    if (which == MODA_KERNEL_TC) {
+        char err[256] = "";
+        r = moda::launch_fwd_tc(p, st, err, sizeof(err));
+        if (r != MODA_OK) return fail(r, "%s", err[0] ? err : "tcgen05 launch failed");
+    } else {
+        r = moda::launch_fwd_simt(p, st);
+        if (r != MODA_OK) return fail(r, "SIMT launch rejected");
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(MODA_ERR_LAUNCH, "CUDA launch error: %s", cudaGetErrorString(e));
+    return MODA_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -129,6 +149,21 @@ int moda_fwd_plan(const ModaTensor* q, const ModaTensor* k, const ModaTensor* v,
     return plan_kernel(p, kernel);
 }
 
+int moda_fwd_lse(const ModaTensor* q, const ModaTensor* k, const ModaTensor* v,
+                 const ModaTensor* kd, const ModaTensor* vd, const ModaTensor* o, float* lse,
+                 int num_layers, float scale, int chunk_size, int dtype, int kernel,
+                 moda_stream_t stream) {
+    g_err[0] = 0;
+    if (chunk_size < 0) return fail(MODA_ERR_ARG, "chunk_size must be >= 0 (0 = none), got %d", chunk_size);
+    moda::FwdParams p;
+    int r = validate_fwd(q, k, v, kd, vd, o, num_layers, scale, dtype, &p);
+    if (r != MODA_OK) return r;
+    if (!lse && static_cast<int64_t>(p.B) * p.Hq * p.T > 0)
+        return fail(MODA_ERR_ARG, "lse must point to B*H_q*T floats");
+    p.lse = lse;
+    return launch_validated(p, kernel, static_cast<cudaStream_t>(stream));
+}
+
 int moda_fwd_ex(const ModaTensor* q, const ModaTensor* k, const ModaTensor* v,
                 const ModaTensor* kd, const ModaTensor* vd, const ModaTensor* o, int num_layers,
                 float scale, int chunk_size, int dtype, int kernel, moda_stream_t stream) {
@@ -137,19 +172,66 @@ int moda_fwd_ex(const ModaTensor* q, const ModaTensor* k, const ModaTensor* v,
     moda::FwdParams p;
     int r = validate_fwd(q, k, v, kd, vd, o, num_layers, scale, dtype, &p);
     if (r != MODA_OK) return r;
-    const int which = plan_kernel(p, kernel);
-    if (which < 0) return which;
-    if (static_cast<int64_t>(p.B) * p.Hq * p.T * p.d == 0) return MODA_OK;  // nothing to write
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-    cudaGetLastError();  // clear a stale error so the check below is ours
-    if (which == MODA_KERNEL_TC) {
-        char err[256] = "";
-        r = moda::launch_fwd_tc(p, st, err, sizeof(err));
-        if (r != MODA_OK) return fail(r, "%s", err[0] ? err : "tcgen05 launch failed");
-    } else {
-        r = moda::launch_fwd_simt(p, st);
-        if (r != MODA_OK) return fail(r, "SIMT launch rejected");
+    p.lse = nullptr;
+    return launch_validated(p, kernel, static_cast<cudaStream_t>(stream));
+}
+
+int64_t moda_bwd_workspace_size(int64_t batch, int64_t num_q_heads, int64_t seq_len) {
+    if (batch < 0 || num_q_heads < 0 || seq_len < 0) return -1;
+    return batch * num_q_heads * seq_len * static_cast<int64_t>(sizeof(float));
+}
+
+int moda_bwd(const ModaTensor* q, const ModaTensor* k, const ModaTensor* v, const ModaTensor* kd,
+             const ModaTensor* vd, const ModaTensor* o, const ModaTensor* dout, const float* lse,
+             const ModaTensor* dq, const ModaTensor* dk, const ModaTensor* dv,
+             const ModaTensor* dkd, const ModaTensor* dvd, void* workspace,
+             int64_t workspace_bytes, int num_layers, float scale, int dtype,
+             moda_stream_t stream) {
+    g_err[0] = 0;
+    moda::FwdParams f;
+    int r = validate_fwd(q, k, v, kd, vd, o, num_layers, scale, dtype, &f);
+    if (r != MODA_OK) return r;
+    if (!dout || !dq || !dk || !dv || !dkd || !dvd) return fail(MODA_ERR_ARG, "null gradient descriptor");
+    const ModaTensor* like[5][2] = {{dout, o}, {dq, q}, {dk, k}, {dv, v}, {dkd, kd}};
+    const char* names[5] = {"dO", "dQ", "dK", "dV", "dK_depth"};
+    for (int i = 0; i < 5; ++i)
+        for (int j = 0; j < 4; ++j)
+            if (like[i][0]->sizes[j] != like[i][1]->sizes[j])
+                return fail(MODA_ERR_SHAPE, "%s must have the shape of its tensor (dim %d: %lld vs %lld)",
+                            names[i], j, (long long)like[i][0]->sizes[j], (long long)like[i][1]->sizes[j]);
+    for (int j = 0; j < 4; ++j)
+        if (dvd->sizes[j] != vd->sizes[j])
+            return fail(MODA_ERR_SHAPE, "dV_depth must have the shape of V_depth");
+    if (kd->sizes[2] != vd->sizes[2])
+        return fail(MODA_ERR_SHAPE, "K_depth and V_depth must have the same number of rows");
+    const int64_t rows = static_cast<int64_t>(f.B) * f.Hq * f.T;
+    if (rows > 0 && !lse) return fail(MODA_ERR_ARG, "lse must point to B*H_q*T floats");
+    if (workspace_bytes < moda_bwd_workspace_size(f.B, f.Hq, f.T) || (rows > 0 && !workspace))
+        return fail(MODA_ERR_ARG, "workspace needs %lld bytes, got %lld",
+                    (long long)moda_bwd_workspace_size(f.B, f.Hq, f.T), (long long)workspace_bytes);
+    const ModaTensor* outs[5] = {dq, dk, dv, dkd, dvd};
+    for (const ModaTensor* t : outs) {
+        int64_t n = 1;
+        for (int j = 0; j < 4; ++j) n *= t->sizes[j];
+        if (n > 0 && !t->ptr) return fail(MODA_ERR_ARG, "a gradient tensor has a null data pointer");
     }
+    if (dout->sizes[0] * dout->sizes[1] * dout->sizes[2] * dout->sizes[3] > 0 && !dout->ptr)
+        return fail(MODA_ERR_ARG, "dO has a null data pointer");
+    if (kd->sizes[2] > 0x7fffffffLL * 4)
+        return fail(MODA_ERR_SHAPE, "depth buffer too large");
+    moda::BwdParams p;
+    p.q = *q; p.k = *k; p.v = *v; p.kd = *kd; p.vd = *vd; p.o = *o; p.dout = *dout;
+    p.dq = *dq; p.dk = *dk; p.dv = *dv; p.dkd = *dkd; p.dvd = *dvd;
+    p.lse = lse;
+    p.delta = static_cast<float*>(workspace);
+    p.B = f.B; p.Hq = f.Hq; p.Hk = f.Hk; p.G = f.G; p.T = f.T; p.d = f.d; p.L = f.L;
+    p.R = kd->sizes[2];
+    p.scale = f.scale;
+    p.dtype = dtype;
+    if (static_cast<int64_t>(p.B) * p.Hk * (p.T + p.R) * p.d == 0) return MODA_OK;
+    cudaGetLastError();
+    r = moda::launch_bwd(p, static_cast<cudaStream_t>(stream));
+    if (r != MODA_OK) return fail(r, "backward launch rejected");
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail(MODA_ERR_LAUNCH, "CUDA launch error: %s", cudaGetErrorString(e));
     return MODA_OK;
@@ -226,6 +308,6 @@ int moda_device_status(moda_stream_t stream) {
     return v;
 }
 
-int moda_version(void) { return 100; }
+int moda_version(void) { return 200; }
 
 }  // extern "C"

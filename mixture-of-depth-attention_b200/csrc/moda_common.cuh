@@ -23,6 +23,7 @@ static __device__ int moda_dev_status = 0;
 #define MODA_DEV __device__ __forceinline__
 
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
 
 // ------------------------------------------------------------------ basics
 MODA_DEV uint32_t smem_u32(const void* p) {

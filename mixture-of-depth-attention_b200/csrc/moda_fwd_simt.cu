@@ -95,6 +95,8 @@ __global__ void __launch_bounds__(kSimtRows * 32)
                 p.vd.strides[3]);
 
     const float inv = 1.f / l;
+    if (p.lse && lane == 0)  // natural log of sum_j exp(scale * q.k_j)
+        p.lse[(static_cast<int64_t>(b) * p.Hq + h) * p.T + t] = (m + __log2f(l)) * kLn2;
     T* o = static_cast<T*>(p.o.ptr) + b * p.o.strides[0] + h * p.o.strides[1] +
            static_cast<int64_t>(t) * p.o.strides[2];
 #pragma unroll

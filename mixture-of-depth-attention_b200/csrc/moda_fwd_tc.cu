@@ -651,6 +651,8 @@ __global__ void __launch_bounds__(kThreads, 1) moda_fwd_tc_kernel(const __grid_c
             const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
             const bool valid = tok < ti.tend;
             const int head = it.hk * p.G + row % p.G;
+            if (p.lse && half == 0 && valid)  // natural log of sum_j exp(scale * q.k_j)
+                p.lse[(static_cast<long long>(it.b) * p.Hq + head) * p.T + tok] = (m_run + __log2f(l_tot)) * kLn2;
             uint4* dst = reinterpret_cast<uint4*>(
                 static_cast<uint16_t*>(p.o) + it.b * p.o_sb + head * p.o_sh +
                 static_cast<long long>(tok) * p.o_st + kHalfD * half);
@@ -842,6 +844,7 @@ int launch_fwd_tc(const FwdParams& p, cudaStream_t stream, char* err, size_t err
     tp.n_tok = n_tok;
     tp.num_pairs = (p.T + 2 * n_tok - 1) / (2 * n_tok);
     tp.sc = p.scale * kLog2e;
+    tp.lse = p.lse;
     const long long items = static_cast<long long>(tp.num_pairs) * p.B * p.Hk;
     if (items == 0) return MODA_OK;
     if (items > 0x7fffffffLL) {

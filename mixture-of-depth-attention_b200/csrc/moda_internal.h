@@ -9,7 +9,20 @@ namespace moda {
 // Validated forward problem. Strides are in elements.
 struct FwdParams {
     ModaTensor q, k, v, kd, vd, o;
+    float* lse;  // optional [B, H_q, T] fp32, contiguous: natural log-sum-exp per row
     int B, Hq, Hk, G, T, d, L;
+    float scale;
+    int dtype;
+};
+
+// Validated backward problem (tensors as in FwdParams, gradients shaped like
+// their inputs). delta is the caller's workspace, [B, H_q, T] fp32.
+struct BwdParams {
+    ModaTensor q, k, v, kd, vd, o, dout, dq, dk, dv, dkd, dvd;
+    const float* lse;
+    float* delta;
+    int B, Hq, Hk, G, T, d, L;
+    long long R;  // depth rows of kd / dkd (>= T*L)
     float scale;
     int dtype;
 };
@@ -30,12 +43,14 @@ struct TcParams {
     int num_pairs;  // tile pairs per (b, kv head)
     int num_items;  // num_pairs * B * Hk work items
     float sc;       // scale * log2(e)
+    float* lse;     // optional [B, H_q, T] fp32 log-sum-exp output
 };
 
 int launch_fwd_simt(const FwdParams& p, cudaStream_t stream);
 int launch_fwd_tc(const FwdParams& p, cudaStream_t stream, char* err, size_t errlen);
 bool tc_supports(const FwdParams& p, char* why, size_t whylen);
 int launch_depth_append(const AppendParams& p, bool vec16, cudaStream_t stream);
+int launch_bwd(const BwdParams& p, cudaStream_t stream);
 cudaError_t read_and_clear_status(cudaStream_t stream, int* value);
 
 }  // namespace moda

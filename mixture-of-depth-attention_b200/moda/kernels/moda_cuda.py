@@ -6,7 +6,8 @@ chunk_size=None)`` keeps the positional/keyword order of
 ``moda_attention_triton`` (moda/kernels/moda_triton.py:218-227) and computes the
 same function: one softmax over the causal sequence keys and the token's own L
 depth rows. The forward always runs in libmoda_b200.so (tcgen05 kernel for
-bf16/f16 with d in {64,128}, CUDA-core kernel otherwise); CPU tensors raise.
+bf16/f16 with d in {64,128}, CUDA-core kernel otherwise), and so does the
+backward (``moda_bwd``, through ``torch.autograd``); CPU tensors raise.
 """
 
 from __future__ import annotations
@@ -78,52 +79,74 @@ def moda_plan(Q, K, V, K_depth, V_depth, num_layers: int, kernel: str = "auto") 
     return {_lib.KERNEL_TC: "tc", _lib.KERNEL_SIMT: "simt"}[code]
 
 
+def moda_forward_lse(Q: Tensor, K: Tensor, V: Tensor, K_depth: Tensor, V_depth: Tensor,
+                     num_layers: int, scale: Optional[float] = None,
+                     chunk_size: Optional[int] = None, kernel: str = "auto"):
+    """Forward that also returns the row log-sum-exp: (O [B,H_q,T,d], lse [B,H_q,T] fp32).
+
+    lse[b,h,t] = log(sum over the row's keys of exp(scale * q.k)), natural log; the
+    backward pass needs it.
+    """
+    _check_inputs(Q, K, V, K_depth, V_depth)
+    O = torch.empty(Q.shape, dtype=Q.dtype, device=Q.device)
+    lse = torch.empty(Q.shape[:3], dtype=torch.float32, device=Q.device)
+    lib = _lib.load()
+    stream = torch.cuda.current_stream(Q.device).cuda_stream
+    with torch.cuda.device(Q.device):
+        code = lib.moda_fwd_lse(_desc(Q), _desc(K), _desc(V), _desc(K_depth), _desc(V_depth),
+                                _desc(O), lse.data_ptr(), int(num_layers),
+                                float(scale) if scale else 0.0, int(chunk_size or 0),
+                                _DTYPES[Q.dtype], _KERNELS[kernel], stream)
+    _lib.check(code, "moda_fwd_lse")
+    return O, lse
+
+
+def moda_backward(dO: Tensor, Q: Tensor, K: Tensor, V: Tensor, K_depth: Tensor,
+                  V_depth: Tensor, O: Tensor, lse: Tensor, num_layers: int,
+                  scale: Optional[float] = None):
+    """Gradients (dQ, dK, dV, dK_depth, dV_depth) of the forward for upstream dO.
+
+    Runs the backward kernels of libmoda_b200.so (moda_bwd); every gradient has the
+    shape and dtype of its input; depth rows the forward never reads get zero.
+    """
+    _check_inputs(Q, K, V, K_depth, V_depth)
+    for n, t in (("dO", dO), ("O", O)):
+        if t.shape != Q.shape or t.dtype != Q.dtype or t.device != Q.device:
+            raise _lib.MoDAShapeError(f"{n} must have Q's shape, dtype and device")
+    if lse.dtype != torch.float32 or lse.shape != Q.shape[:3] or not lse.is_contiguous():
+        raise _lib.MoDAShapeError("lse must be a contiguous float32 [B, H_q, T] tensor")
+    grads = [torch.empty(t.shape, dtype=t.dtype, device=t.device) for t in (Q, K, V, K_depth, V_depth)]
+    lib = _lib.load()
+    nbytes = lib.moda_bwd_workspace_size(Q.shape[0], Q.shape[1], Q.shape[2])
+    work = torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=Q.device)
+    stream = torch.cuda.current_stream(Q.device).cuda_stream
+    with torch.cuda.device(Q.device):
+        code = lib.moda_bwd(_desc(Q), _desc(K), _desc(V), _desc(K_depth), _desc(V_depth),
+                            _desc(O), _desc(dO), lse.data_ptr(), *[_desc(g) for g in grads],
+                            work.data_ptr(), int(nbytes), int(num_layers),
+                            float(scale) if scale else 0.0, _DTYPES[Q.dtype], stream)
+    _lib.check(code, "moda_bwd")
+    return tuple(grads)
+
+
 class _MoDAFunction(torch.autograd.Function):
-    """Forward in libmoda_b200.so. Backward recomputes the attention weights with
-    PyTorch ops on the same CUDA device (not a tuned kernel: the forward is the
-    product here; a fused backward kernel is not built yet)."""
+    """Forward and backward both run in libmoda_b200.so: the forward saves O and the
+    row log-sum-exp; the backward kernels recompute the attention weights from them."""
 
     @staticmethod
     def forward(ctx, Q, K, V, K_depth, V_depth, num_layers, scale, chunk_size, kernel):
-        O = torch.empty(Q.shape, dtype=Q.dtype, device=Q.device)
-        moda_forward_into(O, Q, K, V, K_depth, V_depth, num_layers, scale, chunk_size, kernel)
-        ctx.save_for_backward(Q, K, V, K_depth, V_depth)
+        O, lse = moda_forward_lse(Q, K, V, K_depth, V_depth, num_layers, scale, chunk_size,
+                                  kernel)
+        ctx.save_for_backward(Q, K, V, K_depth, V_depth, O, lse)
         ctx.num_layers = num_layers
         ctx.scale = scale
         return O
 
     @staticmethod
     def backward(ctx, dO):
-        Q, K, V, Kd, Vd = ctx.saved_tensors
-        with torch.enable_grad():
-            ins = [t.detach().float().requires_grad_(True) for t in (Q, K, V, Kd, Vd)]
-            out = _recompute(*ins, ctx.num_layers, ctx.scale)
-            grads = torch.autograd.grad(out, ins, dO.float())
-        return (*[g.to(t.dtype) for g, t in zip(grads, (Q, K, V, Kd, Vd))],
-                None, None, None, None)
-
-
-def _recompute(Q, K, V, Kd, Vd, L, scale):
-    """Differentiable restatement of the forward (fp32, GQA by index, rows [0, T*L) of depth)."""
-    B, H_q, T, d = Q.shape
-    H_k = K.shape[1]
-    G = H_q // H_k
-    s = scale if scale else d ** -0.5
-    Qg = Q.view(B, H_k, G, T, d)
-    s_seq = torch.einsum("bhgtd,bhsd->bhgts", Qg, K) * s
-    causal = torch.ones(T, T, dtype=torch.bool, device=Q.device).triu(1)
-    s_seq = s_seq.masked_fill(causal, float("-inf"))
-    parts = [s_seq]
-    if L > 0:
-        kd = Kd[:, :, :T * L].reshape(B, H_k, T, L, d)
-        s_dep = torch.einsum("bhgtd,bhtld->bhgtl", Qg, kd) * s
-        parts.append(s_dep)
-    w = torch.softmax(torch.cat(parts, dim=-1), dim=-1)
-    out = torch.einsum("bhgts,bhsd->bhgtd", w[..., :T], V)
-    if L > 0:
-        vd = Vd[:, :, :T * L].reshape(B, H_k, T, L, d)
-        out = out + torch.einsum("bhgtl,bhtld->bhgtd", w[..., T:], vd)
-    return out.reshape(B, H_q, T, d)
+        Q, K, V, Kd, Vd, O, lse = ctx.saved_tensors
+        grads = moda_backward(dO, Q, K, V, Kd, Vd, O, lse, ctx.num_layers, ctx.scale)
+        return (*grads, None, None, None, None)
 
 
 def moda_attention_cuda(Q: Tensor, K: Tensor, V: Tensor, K_depth: Tensor, V_depth: Tensor,

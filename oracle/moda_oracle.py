@@ -1,4 +1,4 @@
-"""CPU oracle for the fused MoDA forward (test infrastructure only).
+"""CPU oracle for the fused MoDA forward and its gradients (test infrastructure only).
 
 This module is the checker, never the product: only ``tests/``,
 ``__graft_entry__.smoke()`` and the CPU-baseline leg of ``bench.py`` import it.
@@ -151,6 +151,66 @@ def moda_row(q, k, v, kd, vd, scale):
     w /= w.sum()
     n = k.shape[0]
     return w[:n] @ v + w[n:] @ vd
+
+
+def moda_attention_grads(Q, K, V, K_depth, V_depth, num_layers, dO, scale=None,
+                         dtype=np.float64):
+    """Gradients of moda_attention_naive (moda_naive.py:13-162) for an upstream dO.
+
+    The reference gets these from torch autograd through the same function; this is
+    the closed form of that backward pass (small shapes: dense score matrices):
+      P = softmax(S), S = scale * q.[K; K_depth rows of the token]   (masked as forward)
+      dP = dO.[V; V_depth]^T,  dS = P * (dP - rowsum(dO * O))
+      dQ = scale * dS.[K; K_depth],  d[K; K_depth] = scale * dS^T.Q,  d[V; V_depth] = P^T.dO
+    with the GQA expansion (moda_naive.py:51-56) undone by summing over the G query
+    heads of each KV head. Depth rows at or beyond T*L are never read and get zero
+    gradient. Returns a dict with O, lse (natural log-sum-exp of the scaled scores,
+    [B,H_q,T]), dQ, dK, dV, dK_depth, dV_depth.
+    """
+    Q = _as(Q, dtype)
+    K = _as(K, dtype)
+    V = _as(V, dtype)
+    Kd = _as(K_depth, dtype)
+    Vd = _as(V_depth, dtype)
+    dO = _as(dO, dtype)
+    B, H_q, T, d = Q.shape
+    H_k = K.shape[1]
+    G = H_q // H_k
+    L = num_layers
+    R = Kd.shape[2]
+    if K.shape[2] != T:
+        raise ValueError("K/V must have T rows")
+    if R < T * L:
+        raise ValueError(f"depth buffer has {R} rows, needs {T * L}")
+    if scale is None:
+        scale = d ** -0.5
+    Kall = np.concatenate([K, Kd[:, :, :T * L]], axis=2)      # [B,H_k,T+T*L,d]
+    Vall = np.concatenate([V, Vd[:, :, :T * L]], axis=2)
+    Ke = np.repeat(Kall, G, axis=1)
+    Ve = np.repeat(Vall, G, axis=1)
+    s = np.matmul(Q, np.swapaxes(Ke, -1, -2)) * scale        # [B,H_q,T,T+T*L]
+    keep_seq = np.arange(T)[None, :] <= np.arange(T)[:, None]
+    keep_dep = (np.arange(T * L) // L)[None, :] == np.arange(T)[:, None]
+    keep = np.concatenate([keep_seq, keep_dep], axis=1)
+    s = np.where(keep[None, None], s, -np.inf)
+    m = np.max(s, axis=-1, keepdims=True)
+    e = np.exp(s - m)
+    l = np.sum(e, axis=-1, keepdims=True)
+    P = e / l
+    O = np.matmul(P, Ve)
+    dP = np.matmul(dO, np.swapaxes(Ve, -1, -2))
+    dS = P * (dP - np.sum(dO * O, axis=-1, keepdims=True))
+    dQ = scale * np.matmul(dS, Ke)
+    dKe = scale * np.matmul(np.swapaxes(dS, -1, -2), Q)      # [B,H_q,T+T*L,d]
+    dVe = np.matmul(np.swapaxes(P, -1, -2), dO)
+    dKall = dKe.reshape(B, H_k, G, T + T * L, d).sum(axis=2)
+    dVall = dVe.reshape(B, H_k, G, T + T * L, d).sum(axis=2)
+    dKd = np.zeros_like(Kd)
+    dVd = np.zeros_like(Vd)
+    dKd[:, :, :T * L] = dKall[:, :, T:]
+    dVd[:, :, :T * L] = dVall[:, :, T:]
+    return dict(O=O, lse=(m + np.log(l))[..., 0], dQ=dQ, dK=dKall[:, :, :T], dV=dVall[:, :, :T],
+                dK_depth=dKd, dV_depth=dVd)
 
 
 def depth_cache_write(k_cache, v_cache, layer_idx, k, v, num_layers, seq_len=None):

@@ -49,6 +49,27 @@ def kernel_case(name, B, H_q, H_k, T, d, L, seed, chunk_sizes, extra_rows=0, sca
     return name, arrays | outs, meta
 
 
+def grad_case(name, B, H_q, H_k, T, d, L, seed, chunk_size, extra_rows=0, scale=None):
+    """The reference's gradients: moda_attention_naive under torch autograd (CPU, fp64)."""
+    from moda.kernels.moda_naive import moda_attention_naive
+    R = T * L + extra_rows
+    g = torch.Generator().manual_seed(seed)
+    shapes = [(B, H_q, T, d), (B, H_k, T, d), (B, H_k, T, d), (B, H_k, R, d), (B, H_k, R, d),
+              (B, H_q, T, d)]
+    # fp32 inputs (stored exactly), fp64 arithmetic, results stored rounded to fp32
+    Q, K, V, Kd, Vd, dO = [torch.randn(*s, generator=g) for s in shapes]
+    leaves = [t.double().requires_grad_(True) for t in (Q, K, V, Kd, Vd)]
+    O = moda_attention_naive(*leaves, num_layers=L, scale=scale, chunk_size=chunk_size)
+    O.backward(dO.double())
+    names = ["Q", "K", "V", "K_depth", "V_depth"]
+    arrays = {n: t.numpy() for n, t in zip(names, (Q, K, V, Kd, Vd))}
+    arrays |= {"dO": dO.numpy(), "O": O.detach().float().numpy()}
+    arrays |= {"d" + n: t.grad.float().numpy() for n, t in zip(names, leaves)}
+    meta = dict(kind="grad", B=B, H_q=H_q, H_k=H_k, T=T, d=d, L=L, seed=seed, scale=scale,
+                depth_rows=R, chunk_size=chunk_size)
+    return name, arrays, meta
+
+
 def module_case():
     from moda.config import MoDAConfig
     from moda.attention import MoDAAttention
@@ -133,6 +154,12 @@ def main():
         kernel_case("s_b1_h4x4_t19_d32_l2_scale", 1, 4, 4, 19, 32, 2, 30, [None, 5], scale=0.3),
         # oversize depth buffer: only rows [0, T*L) are addressed; unchunked form raises
         kernel_case("o_b1_h4x2_t20_d64_l4_extra16", 1, 4, 2, 20, 64, 4, 31, [None, 8], extra_rows=16),
+        # gradients (torch autograd through the reference, fp64)
+        grad_case("grad_b1_h4x2_t32_d64_l8", 1, 4, 2, 32, 64, 8, 40, 8),
+        grad_case("grad_b2_h2x2_t16_d32_l4", 2, 2, 2, 16, 32, 4, 41, None),
+        grad_case("grad_b1_h8x2_t20_d64_l3_extra8", 1, 8, 2, 20, 64, 3, 42, 16, extra_rows=8),
+        grad_case("grad_b1_h16x2_t12_d64_l48", 1, 16, 2, 12, 64, 48, 43, None),
+        grad_case("grad_b1_h4x1_t9_d16_l5_scale", 1, 4, 1, 9, 16, 5, 44, 4, scale=0.4),
         module_case(),
         model_case(True),
         model_case(False),
@@ -140,7 +167,8 @@ def main():
     ]
     for name, arrays, meta in cases:
         meta["torch"] = torch.__version__
-        meta["source"] = "reference moda (sahilmalik27/mixture-of-depth-attention), CPU fp32"
+        meta["source"] = ("reference moda (sahilmalik27/mixture-of-depth-attention), CPU "
+                          + ("fp64 autograd" if meta["kind"] == "grad" else "fp32"))
         path = os.path.join(HERE, name + ".npz")
         np.savez_compressed(path, meta=np.array(json.dumps(meta)), **arrays)
         print(f"{name}: {os.path.getsize(path)} bytes, keys={sorted(arrays)[:8]}...")

@@ -28,7 +28,7 @@ def test_library_exports_every_declared_symbol():
     lib = _lib.load()
     for name in declared_functions():
         assert hasattr(lib, name), name
-    assert lib.moda_version() == 100
+    assert lib.moda_version() == 200
     assert lib.moda_last_error() == b""
 
 
@@ -113,3 +113,47 @@ def test_cpu_tensors_are_refused_by_the_kernel_entry():
     x = torch.zeros(1, 2, 4, 16)
     with pytest.raises(RuntimeError, match="CUDA"):
         moda_attention_cuda(x, x, x, torch.zeros(1, 2, 8, 16), torch.zeros(1, 2, 8, 16), 2)
+
+
+def _bwd_args(B=1, Hq=4, Hk=2, T=8, d=16, L=2, R=None, dq_shape=None, work=1 << 20):
+    """moda_bwd arguments over host tensors. Every call below fails validation, so
+    nothing is launched (and no host pointer ever reaches a kernel)."""
+    R = T * L if R is None else R
+    Q, O, dO = _t((B, Hq, T, d)), _t((B, Hq, T, d)), _t((B, Hq, T, d))
+    K, V = _t((B, Hk, T, d)), _t((B, Hk, T, d))
+    Kd, Vd = _t((B, Hk, R, d)), _t((B, Hk, R, d))
+    dQ = _t(dq_shape or (B, Hq, T, d))
+    dK, dV, dKd, dVd = _t((B, Hk, T, d)), _t((B, Hk, T, d)), _t((B, Hk, R, d)), _t((B, Hk, R, d))
+    lse = torch.empty(B, Hq, T)
+    ws = torch.empty(work, dtype=torch.uint8)
+    keep = (Q, O, dO, K, V, Kd, Vd, dQ, dK, dV, dKd, dVd, lse, ws)
+    D = lambda x: _lib.describe(x.data_ptr(), x.shape, x.stride())
+    args = [D(Q), D(K), D(V), D(Kd), D(Vd), D(O), D(dO), lse.data_ptr(), D(dQ), D(dK), D(dV),
+            D(dKd), D(dVd), ws.data_ptr(), work, L, 0.0, _lib.MODA_BF16, None]
+    return args, keep
+
+
+def test_bwd_workspace_size():
+    lib = _lib.load()
+    assert lib.moda_bwd_workspace_size(2, 8, 100) == 2 * 8 * 100 * 4
+    assert lib.moda_bwd_workspace_size(-1, 8, 100) == -1
+
+
+@pytest.mark.parametrize("case", ["dq_shape", "short_depth", "small_workspace", "null_lse"])
+def test_bwd_rejects_bad_arguments_before_launch(case):
+    lib = _lib.load()
+    if case == "dq_shape":
+        args, keep = _bwd_args(dq_shape=(1, 4, 7, 16))
+        expect = _lib.MODA_ERR_SHAPE
+    elif case == "short_depth":
+        args, keep = _bwd_args(R=10)
+        expect = _lib.MODA_ERR_DEPTH_ROWS
+    elif case == "small_workspace":
+        args, keep = _bwd_args(work=4 * 4 * 8 - 4)
+        expect = _lib.MODA_ERR_ARG
+    else:
+        args, keep = _bwd_args()
+        args[7] = None
+        expect = _lib.MODA_ERR_ARG
+    assert lib.moda_bwd(*args) == expect
+    assert lib.moda_last_error() != b""

@@ -1,0 +1,145 @@
+"""Parity of the CUDA backward (moda_bwd via the C ABI) with the reference's gradients.
+
+The golden gradient fixtures hold torch autograd through the reference's
+moda_attention_naive (fp64, tests/golden/make_golden.py); the oracle's closed
+form (oracle/moda_oracle.py: moda_attention_grads) is pinned to them on CPU.
+
+Tolerances:
+  fp32 inputs: max|g - ref| / max|ref| <= 1e-4 for every gradient   (FP32_REL_TOL)
+  bf16/f16 inputs (gradients stored in that dtype), against the fp64 oracle on the
+  same rounded inputs: max|g - ref| <= 2e-2 * max(1, max|ref|)       (BF16_ABS_TOL)
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from moda.kernels import device_status, moda_attention_cuda, moda_backward, moda_forward_lse
+from oracle import moda_oracle as orc
+from helpers import BF16_ABS_TOL, FP32_REL_TOL, golden_cases, rel_err, seeded_inputs
+
+pytestmark = pytest.mark.gpu
+GRAD_CASES = golden_cases("grad")
+NAMES = ("Q", "K", "V", "K_depth", "V_depth")
+GRADS = ("dQ", "dK", "dV", "dK_depth", "dV_depth")
+
+
+def dev(arrs, dtype):
+    return [torch.from_numpy(np.ascontiguousarray(a)).to("cuda", dtype) for a in arrs]
+
+
+def rounded(arrs, dtype):
+    return [torch.from_numpy(np.ascontiguousarray(a)).to(dtype).double().numpy() for a in arrs]
+
+
+def host(t):
+    return t.double().cpu().numpy()
+
+
+def half_ok(g, ref):
+    return float(np.max(np.abs(g - ref))) <= BF16_ABS_TOL * max(1.0, float(np.max(np.abs(ref))))
+
+
+@pytest.fixture(autouse=True)
+def _no_device_timeouts():
+    yield
+    assert device_status() == 0, "a bounded device wait expired"
+
+
+@pytest.mark.parametrize("name,z,meta", GRAD_CASES, ids=[c[0] for c in GRAD_CASES])
+def test_golden_grads_fp32(name, z, meta):
+    ins = dev([z[k] for k in NAMES], torch.float32)
+    O, lse = moda_forward_lse(*ins, meta["L"], meta["scale"])
+    dO = dev([z["dO"]], torch.float32)[0]
+    grads = moda_backward(dO, *ins, O, lse, meta["L"], meta["scale"])
+    torch.cuda.synchronize()
+    assert rel_err(host(O), z["O"]) <= FP32_REL_TOL
+    ref = orc.moda_attention_grads(*[z[k] for k in NAMES], meta["L"], z["dO"], scale=meta["scale"])
+    assert float(np.max(np.abs(host(lse) - ref["lse"]))) <= 1e-4
+    for g, k in zip(grads, GRADS):
+        assert g.shape == ins[GRADS.index(k)].shape and g.dtype == torch.float32
+        assert rel_err(host(g), z[k]) <= FP32_REL_TOL, (k, rel_err(host(g), z[k]))
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "f16"])
+@pytest.mark.parametrize("name,z,meta", GRAD_CASES, ids=[c[0] for c in GRAD_CASES])
+def test_golden_grads_half(name, z, meta, dtype):
+    arrs = [z[k] for k in NAMES]
+    rin = rounded(arrs + [z["dO"]], dtype)
+    ref = orc.moda_attention_grads(*rin[:5], meta["L"], rin[5], scale=meta["scale"])
+    ins = dev(arrs, dtype)
+    dO = dev([z["dO"]], dtype)[0]
+    for kernel in ("auto", "simt"):   # forward on the tcgen05 kernel where it tiles
+        O, lse = moda_forward_lse(*ins, meta["L"], meta["scale"], kernel=kernel)
+        grads = moda_backward(dO, *ins, O, lse, meta["L"], meta["scale"])
+        torch.cuda.synchronize()
+        assert float(np.max(np.abs(host(lse) - ref["lse"]))) <= 1e-2, kernel
+        for g, k in zip(grads, GRADS):
+            assert g.dtype == dtype
+            assert half_ok(host(g), ref[k]), (kernel, k, float(np.max(np.abs(host(g) - ref[k]))))
+
+
+def test_medium_shape_bf16():
+    """B=1, H_q=8, H_k=2 (GQA 4), T=256, d=128, L=4: the tcgen05 forward's tiling and
+    several causal blocks, against the oracle."""
+    L = 4
+    arrs = seeded_inputs(1, 8, 2, 256, 128, L, seed=50)
+    dO = np.random.default_rng(51).standard_normal((1, 8, 256, 128)).astype(np.float32)
+    rin = rounded(arrs + [dO], torch.bfloat16)
+    ref = orc.moda_attention_grads(*rin[:5], L, rin[5])
+    ins = dev(arrs, torch.bfloat16)
+    O, lse = moda_forward_lse(*ins, L, kernel="tc")
+    grads = moda_backward(dev([dO], torch.bfloat16)[0], *ins, O, lse, L)
+    torch.cuda.synchronize()
+    for g, k in zip(grads, GRADS):
+        assert half_ok(host(g), ref[k]), (k, float(np.max(np.abs(host(g) - ref[k]))))
+
+
+def test_autograd_through_moda_attention_cuda():
+    """Reference tests/test_kernel.py:106-119: out.sum().backward() gives finite
+    gradients for all five inputs (dO is then a zero-stride expanded tensor)."""
+    B, H, T, L, d = 1, 2, 4, 2, 8
+    arrs = seeded_inputs(B, H, H, T, d, L, seed=52)
+    ins = [t.requires_grad_(True) for t in dev(arrs, torch.float32)]
+    out = moda_attention_cuda(*ins, num_layers=L)
+    out.sum().backward()
+    ref = orc.moda_attention_grads(*arrs, L, np.ones((B, H, T, d)))
+    for t, k in zip(ins, GRADS):
+        assert t.grad is not None and torch.isfinite(t.grad).all(), k
+        assert rel_err(host(t.grad), ref[k]) <= FP32_REL_TOL, k
+
+
+def test_autograd_matches_direct_backward_with_strided_views():
+    """MoDAAttention hands the kernel transposed views; gradients flow back into them."""
+    B, Hq, Hk, T, d, L = 2, 4, 2, 24, 64, 3
+    arrs = seeded_inputs(B, Hq, Hk, T, d, L, seed=53)
+    q_bthd = torch.from_numpy(np.ascontiguousarray(arrs[0].transpose(0, 2, 1, 3))).cuda().bfloat16()
+    q_bthd.requires_grad_(True)
+    rest = [t.requires_grad_(True) for t in dev(arrs[1:], torch.bfloat16)]
+    Q = q_bthd.transpose(1, 2)                       # strides (T*H*d, d, H*d, 1)
+    out = moda_attention_cuda(Q, *rest, num_layers=L)
+    W = torch.randn(out.shape, device="cuda", generator=torch.Generator("cuda").manual_seed(54))
+    (out.float() * W).sum().backward()
+    rin = rounded(arrs, torch.bfloat16)
+    ref = orc.moda_attention_grads(*rin, L, W.double().cpu().numpy())
+    assert half_ok(host(q_bthd.grad.transpose(1, 2)), ref["dQ"])
+    for t, k in zip(rest, GRADS[1:]):
+        assert half_ok(host(t.grad), ref[k]), k
+
+
+def test_module_gradient_through_depth():
+    """Reference tests/test_attention.py:57-71 on CUDA: gradients reach x, K_depth, V_depth."""
+    from moda.config import MoDAConfig
+    from moda.attention import MoDAAttention
+    torch.manual_seed(55)
+    cfg = MoDAConfig(d_model=64, num_heads=4, num_kv_heads=2, num_layers=3)
+    attn = MoDAAttention(cfg).cuda()
+    B, T, L = 1, 4, 3
+    x = torch.randn(B, T, cfg.d_model, device="cuda", requires_grad=True)
+    Kd = torch.randn(B, cfg.num_kv_heads, T * L, cfg.head_dim, device="cuda", requires_grad=True)
+    Vd = torch.randn(B, cfg.num_kv_heads, T * L, cfg.head_dim, device="cuda", requires_grad=True)
+    out, _, _ = attn(x, Kd, Vd)
+    out.sum().backward()
+    for t in (x, Kd, Vd):
+        assert t.grad is not None and torch.isfinite(t.grad).all()
+        assert float(t.grad.abs().max()) > 0

@@ -97,3 +97,35 @@ def test_roofline_formulas():
     by = orc.hbm_bytes(4, 32, 8, 8192, 128, 32, 2)
     assert abs(f / 1e12 - 2.2165) < 1e-3
     assert abs(by / 1e9 - 4.966) < 1e-3
+
+
+GRAD_CASES = golden_cases("grad")
+GRAD_KEYS = ("O", "dQ", "dK", "dV", "dK_depth", "dV_depth")
+
+
+@pytest.mark.parametrize("name,z,meta", GRAD_CASES, ids=[c[0] for c in GRAD_CASES])
+def test_grad_oracle_matches_reference_autograd(name, z, meta):
+    """The closed-form backward equals torch autograd through the reference (fp64)."""
+    r = orc.moda_attention_grads(z["Q"], z["K"], z["V"], z["K_depth"], z["V_depth"], meta["L"],
+                                 z["dO"], scale=meta["scale"])
+    for k in GRAD_KEYS:
+        ref = z[k].astype(np.float64)
+        assert r[k].shape == ref.shape, k
+        assert max_abs(r[k], ref) <= 1e-6 * max(1.0, float(np.max(np.abs(ref)))), k
+    if meta["depth_rows"] > meta["T"] * meta["L"]:
+        # rows past T*L are never read: zero gradient, as in the reference
+        assert not np.any(z["dK_depth"][:, :, meta["T"] * meta["L"]:])
+
+
+def test_grad_oracle_lse_matches_forward():
+    z, meta = GRAD_CASES[0][1], GRAD_CASES[0][2]
+    r = orc.moda_attention_grads(z["Q"], z["K"], z["V"], z["K_depth"], z["V_depth"], meta["L"],
+                                 z["dO"], scale=meta["scale"])
+    o = orc.moda_attention_naive(z["Q"], z["K"], z["V"], z["K_depth"], z["V_depth"], meta["L"],
+                                 scale=meta["scale"])
+    assert max_abs(r["O"], o) < 1e-12
+    # lse row by row from the single-row form
+    f64 = lambda a: np.asarray(a, np.float64)
+    q, k, kd = f64(z["Q"][0, 1, 5]), f64(z["K"][0, 0, :6]), f64(z["K_depth"][0, 0, 5 * meta["L"]:6 * meta["L"]])
+    s = np.concatenate([k @ q, kd @ q]) * z["Q"].shape[-1] ** -0.5
+    assert abs(r["lse"][0, 1, 5] - (s.max() + np.log(np.exp(s - s.max()).sum()))) < 1e-9
