@@ -103,6 +103,23 @@ int moda_bwd(const ModaTensor* q, const ModaTensor* k, const ModaTensor* v, cons
              int64_t workspace_bytes, int num_layers, float scale, int dtype,
              moda_stream_t stream);
 
+/* Largest B*H_q*T that moda_bwd_noalloc accepts. */
+#define MODA_NOALLOC_ROWS (1 << 20)
+
+/* moda_bwd without any workspace argument: the rowsum(dO*O) scratch is a fixed
+ * array compiled into the library (MODA_NOALLOC_ROWS floats per device, its address
+ * resolved once per device), so the call allocates nothing and needs no buffer from
+ * the caller. B*H_q*T > MODA_NOALLOC_ROWS is rejected with MODA_ERR_UNSUPPORTED
+ * before anything else. The array is shared by all calls on a device: such calls
+ * must not overlap in time (issue them on one stream, or synchronize).
+ * No reference counterpart (the reference's autograd allocates through torch). */
+int moda_bwd_noalloc(const ModaTensor* q, const ModaTensor* k, const ModaTensor* v,
+                     const ModaTensor* kd, const ModaTensor* vd, const ModaTensor* o,
+                     const ModaTensor* dout, const float* lse, const ModaTensor* dq,
+                     const ModaTensor* dk, const ModaTensor* dv, const ModaTensor* dkd,
+                     const ModaTensor* dvd, int num_layers, float scale, int dtype,
+                     moda_stream_t stream);
+
 /* Which kernel moda_fwd_ex would launch for these arguments (ModaKernel value,
  * or a negative ModaStatus). Host-only: validates and plans, launches nothing.
  * No reference counterpart (the reference picks its path in Python,

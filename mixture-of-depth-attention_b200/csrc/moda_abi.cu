@@ -181,6 +181,28 @@ int64_t moda_bwd_workspace_size(int64_t batch, int64_t num_q_heads, int64_t seq_
     return batch * num_q_heads * seq_len * static_cast<int64_t>(sizeof(float));
 }
 
+int moda_bwd_noalloc(const ModaTensor* q, const ModaTensor* k, const ModaTensor* v,
+                     const ModaTensor* kd, const ModaTensor* vd, const ModaTensor* o,
+                     const ModaTensor* dout, const float* lse, const ModaTensor* dq,
+                     const ModaTensor* dk, const ModaTensor* dv, const ModaTensor* dkd,
+                     const ModaTensor* dvd, int num_layers, float scale, int dtype,
+                     moda_stream_t stream) {
+    g_err[0] = 0;
+    // Size check first, before anything else touches the descriptors or CUDA.
+    if (!q) return fail(MODA_ERR_ARG, "null tensor descriptor");
+    const int64_t rows = q->sizes[0] * q->sizes[1] * q->sizes[2];
+    if (q->sizes[0] < 0 || q->sizes[1] < 0 || q->sizes[2] < 0 || rows > MODA_NOALLOC_ROWS)
+        return fail(MODA_ERR_UNSUPPORTED,
+                    "moda_bwd_noalloc handles up to %d query rows (B*H_q*T), got %lld",
+                    MODA_NOALLOC_ROWS, (long long)rows);
+    void* scratch = nullptr;
+    if (rows > 0 && moda::noalloc_scratch(&scratch) != cudaSuccess)
+        return fail(MODA_ERR_LAUNCH, "could not resolve the library's backward scratch");
+    return moda_bwd(q, k, v, kd, vd, o, dout, lse, dq, dk, dv, dkd, dvd, scratch,
+                    static_cast<int64_t>(MODA_NOALLOC_ROWS) * static_cast<int64_t>(sizeof(float)),
+                    num_layers, scale, dtype, stream);
+}
+
 int moda_bwd(const ModaTensor* q, const ModaTensor* k, const ModaTensor* v, const ModaTensor* kd,
              const ModaTensor* vd, const ModaTensor* o, const ModaTensor* dout, const float* lse,
              const ModaTensor* dq, const ModaTensor* dk, const ModaTensor* dv,

@@ -24,6 +24,8 @@
 // fp32 arithmetic throughout; inputs and gradients in the forward's dtype.
 #include "moda_internal.h"
 
+#include <mutex>
+
 namespace moda {
 
 namespace {
@@ -223,6 +225,26 @@ static void launch_bwd_t(const BwdParams& p, cudaStream_t stream) {
         const dim3 gd(static_cast<unsigned>((p.R + kRows - 1) / kRows), p.Hk, p.B);
         moda_bwd_dkdv_kernel<T, true><<<gd, block, 0, stream>>>(p);
     }
+}
+
+// Scratch for moda_bwd_noalloc: rowsum(dO * O) of up to MODA_NOALLOC_ROWS query rows,
+// part of the library image, so that entry point allocates nothing.
+static __device__ __align__(256) float g_noalloc_delta[MODA_NOALLOC_ROWS];
+
+cudaError_t noalloc_scratch(void** ptr) {
+    static std::mutex mu;
+    static void* addr[kMaxDevices] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+        e = cudaGetSymbolAddress(&addr[dev], g_noalloc_delta);  // once per device
+        if (e != cudaSuccess) return e;
+    }
+    *ptr = addr[dev];
+    return cudaSuccess;
 }
 
 int launch_bwd(const BwdParams& p, cudaStream_t stream) {

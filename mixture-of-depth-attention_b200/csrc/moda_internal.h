@@ -51,6 +51,9 @@ int launch_fwd_tc(const FwdParams& p, cudaStream_t stream, char* err, size_t err
 bool tc_supports(const FwdParams& p, char* why, size_t whylen);
 int launch_depth_append(const AppendParams& p, bool vec16, cudaStream_t stream);
 int launch_bwd(const BwdParams& p, cudaStream_t stream);
+constexpr int kMaxDevices = 64;
+// Device address of the library's fixed backward scratch on the current device.
+cudaError_t noalloc_scratch(void** ptr);
 cudaError_t read_and_clear_status(cudaStream_t stream, int* value);
 
 }  // namespace moda

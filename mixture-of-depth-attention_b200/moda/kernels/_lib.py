@@ -22,8 +22,9 @@ MODA_ERR_DTYPE, MODA_ERR_LAUNCH, MODA_ERR_UNSUPPORTED = -4, -5, -6
 KERNEL_AUTO, KERNEL_TC, KERNEL_SIMT = 0, 1, 2
 
 EXPORTED_SYMBOLS = ("moda_fwd", "moda_fwd_ex", "moda_fwd_lse", "moda_fwd_plan", "moda_bwd",
-                    "moda_bwd_workspace_size", "moda_depth_append", "moda_last_error",
-                    "moda_device_status", "moda_version")
+                    "moda_bwd_noalloc", "moda_bwd_workspace_size", "moda_depth_append",
+                    "moda_last_error", "moda_device_status", "moda_version")
+NOALLOC_ROWS = 1 << 20   # MODA_NOALLOC_ROWS
 
 
 class ModaTensor(ctypes.Structure):
@@ -67,6 +68,8 @@ def load():
         lib.moda_bwd_workspace_size.restype = i64
         lib.moda_bwd.argtypes = [T] * 7 + [vp] + [T] * 5 + [vp, i64, i, f, i, vp]
         lib.moda_bwd.restype = i
+        lib.moda_bwd_noalloc.argtypes = [T] * 7 + [vp] + [T] * 5 + [i, f, i, vp]
+        lib.moda_bwd_noalloc.restype = i
         lib.moda_fwd_plan.argtypes = [T, T, T, T, T, T, i, i, i]
         lib.moda_fwd_plan.restype = i
         lib.moda_depth_append.argtypes = [T, T, T, T, i, i, i, i, vp]
