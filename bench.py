@@ -1,7 +1,7 @@
 """Benchmark of the fused MoDA forward on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload kernel|scaling]
+                    [--workload kernel|scaling] [--pass forward|backward]
 
 One step = one fused forward over one batch of synthetic N(0,1) inputs already
 resident in HBM. Default workload (per GPU): the kernel-only configuration
@@ -18,6 +18,11 @@ public API with pinned host buffers and H2D/D2H copies inside the timed
 region), cpu_baseline (the numpy oracle port of moda_attention_naive timed on
 this host on a bounded sample), clocks sampled during the timed region, and
 gpu_launches. ``--impl reference`` times that CPU port alone on rank 0.
+
+``--pass backward`` (one GPU) times the backward kernels instead: one step = the
+gradients of all five inputs for a seeded dO, from the forward's O and row
+log-sum-exp (computed once, untimed). Its algorithmic FLOPs are 2.5x the
+forward's (S recomputed, dP, dQ, dK, dV: five d-long products per attended pair).
 """
 
 from __future__ import annotations
@@ -48,6 +53,7 @@ WORKLOADS = {
                          "L=48 chunk_size=128, batch split over GPUs"),
 }
 METRIC = "MoDA fused seq+depth attention forward throughput (TFLOP/s)"
+METRIC_BWD = "MoDA fused seq+depth attention backward throughput (TFLOP/s)"
 
 
 def flops(B, Hq, T, d, L):
@@ -207,10 +213,13 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="kernel")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--pass", dest="which", choices=["forward", "backward"], default="forward")
     args = ap.parse_args()
     wl = WORKLOADS[args.workload]
     if args.impl == "reference":
         return run_reference(args, wl)
+    if args.which == "backward":
+        return run_backward(args, wl)
     args.warmup = max(args.warmup, 3)
 
     import torch
@@ -363,6 +372,57 @@ def main():
         "clocks": clocks.summary(),
         "verify": {"finite": finite_all, "device_status": status,
                    "checksums": [float(g[0].item()) for g in gathered]},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_backward(args, wl):
+    """Backward kernels alone on one GPU (see the module docstring)."""
+    import torch
+    from moda.kernels import device_status
+    from moda.kernels.moda_cuda import moda_backward, moda_forward_lse
+    args.warmup = max(args.warmup, 3)
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B, Hq, Hk, T, d, L, C = wl["B"], wl["Hq"], wl["Hk"], wl["T"], wl["d"], wl["L"], wl["chunk"]
+    Q, K, V, Kd, Vd = make_inputs(wl, 0, B, dev, torch.bfloat16)
+    O, lse = moda_forward_lse(Q, K, V, Kd, Vd, L, None, C)
+    g = torch.Generator(device=dev).manual_seed(wl["seed"] + 7)
+    dO = torch.randn(Q.shape, device=dev, dtype=torch.bfloat16, generator=g)
+
+    def step():
+        return moda_backward(dO, Q, K, V, Kd, Vd, O, lse, L)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    stream = torch.cuda.current_stream(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clocks:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            grads = step()
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+    ms_step = ev0.elapsed_time(ev1) / args.steps
+    f_bwd = 2.5 * flops(B, Hq, T, d, L)
+    tflops = f_bwd / (ms_step * 1e-3) / 1e12
+    p_tflops, p_gbs, p_kind = peaks()
+    finite = all(bool(torch.isfinite(x).all()) for x in grads)
+    line = {
+        "metric": METRIC_BWD, "value": tflops, "unit": "TFLOP/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic N(0,1), seeded per batch; dO seeded N(0,1)",
+        "config": {"workload": wl["desc"].replace("forward", "backward"), "global_batch": B,
+                   "H_q": Hq, "H_k": Hk, "seq_len": T, "head_dim": d, "num_layers": L},
+        "roofline": {"bound": "tensor", "achieved": tflops, "peak": p_tflops, "unit": "TFLOP/s",
+                     "frac": tflops / p_tflops, "peak_kind": p_kind, "traffic": None,
+                     "algorithmic_flops": f_bwd,
+                     "note": "CUDA-core kernels (fp32 FMA); the tensor-core peak is the target"},
+        "gpu_launches": 4 * args.steps,
+        "clocks": clocks.summary(),
+        "verify": {"finite": finite, "device_status": device_status(dev)},
     }
     print(json.dumps(line), flush=True)
 

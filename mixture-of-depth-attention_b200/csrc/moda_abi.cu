@@ -252,8 +252,9 @@ int moda_bwd(const ModaTensor* q, const ModaTensor* k, const ModaTensor* v, cons
     p.dtype = dtype;
     if (static_cast<int64_t>(p.B) * p.Hk * (p.T + p.R) * p.d == 0) return MODA_OK;
     cudaGetLastError();
-    r = moda::launch_bwd(p, static_cast<cudaStream_t>(stream));
-    if (r != MODA_OK) return fail(r, "backward launch rejected");
+    char err[256] = "";
+    r = moda::launch_bwd(p, static_cast<cudaStream_t>(stream), err, sizeof(err));
+    if (r != MODA_OK) return fail(r, "%s", err[0] ? err : "backward launch rejected");
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail(MODA_ERR_LAUNCH, "CUDA launch error: %s", cudaGetErrorString(e));
     return MODA_OK;
@@ -324,10 +325,11 @@ int moda_depth_append(const ModaTensor* k_src, const ModaTensor* v_src, const Mo
 const char* moda_last_error(void) { return g_err; }
 
 int moda_device_status(moda_stream_t stream) {
-    int v = 0;
-    if (moda::read_and_clear_status(static_cast<cudaStream_t>(stream), &v) != cudaSuccess)
+    int v = 0, w = 0;
+    if (moda::read_and_clear_status(static_cast<cudaStream_t>(stream), &v) != cudaSuccess ||
+        moda::read_and_clear_bwd_status(static_cast<cudaStream_t>(stream), &w) != cudaSuccess)
         return fail(MODA_ERR_LAUNCH, "could not read the device status word");
-    return v;
+    return v ? v : w;
 }
 
 int moda_version(void) { return 200; }

@@ -247,7 +247,24 @@ cudaError_t noalloc_scratch(void** ptr) {
     return cudaSuccess;
 }
 
-int launch_bwd(const BwdParams& p, cudaStream_t stream) {
+template <typename T>
+static void launch_delta_t(const BwdParams& p, cudaStream_t stream) {
+    const dim3 gq((p.T + kRows - 1) / kRows, p.Hq, p.B);
+    moda_bwd_delta_kernel<T><<<gq, dim3(kRows * 32), 0, stream>>>(p);
+}
+
+// bf16/f16 with d in {64, 128}, H_q/H_k dividing 128 and TMA-friendly layouts: the
+// sequence part on tensor cores (moda_bwd_tc.cu) and the depth part per token;
+// everything else (fp32 included) on the CUDA-core kernels above.
+int launch_bwd(const BwdParams& p, cudaStream_t stream, char* err, size_t errlen) {
+    char why[160];
+    if (tc_bwd_supports(p, why, sizeof(why))) {
+        if (p.dtype == MODA_BF16) launch_delta_t<__nv_bfloat16>(p, stream);
+        else launch_delta_t<__half>(p, stream);
+        int r = launch_bwd_tc(p, stream, err, errlen);
+        if (r != MODA_OK) return r;
+        return launch_bwd_depth(p, stream);
+    }
     switch (p.dtype) {
         case MODA_F32: launch_bwd_t<float>(p, stream); break;
         case MODA_BF16: launch_bwd_t<__nv_bfloat16>(p, stream); break;

@@ -1,0 +1,678 @@
+// MoDA backward on Blackwell tensor cores (sequence part) + a per-token CUDA-core
+// kernel for the depth part.
+//
+// Gradients of the fused forward (moda/kernels/moda_naive.py:13-162 under torch
+// autograd): with P = exp(scale*Q.K^T - lse) (row lse from the forward) and
+// D = rowsum(dO * O),
+//   dS = P * (dO.V^T - D),  dQ = scale*dS.K,  dK = scale*dS^T.Q,  dV = P^T.dO.
+//
+// Two launches of one kernel template, each a persistent TMA -> tcgen05.mma ->
+// TMEM pipeline like the forward's:
+//   MODE_DKDV  work item = 128 keys of one (batch, KV head). For every 128-row
+//              query tile (token-major, the G query heads of the KV head) that
+//              reaches those keys: S^T = K.Q^T and dP^T = V.dO^T into TMEM; four
+//              warps (one key row per thread) form P^T and dS^T in 16-bit and
+//              write them back into TMEM; dV += P^T.dO and dK += dS^T.Q take A
+//              from TMEM. dK and dV accumulate in TMEM over all query tiles, so
+//              the GQA sum over heads needs no atomics.
+//   MODE_DQ    work item = one 128-row query tile. For every 128-key block up to
+//              the diagonal: S = Q.K^T, dP = dO.V^T, dS (one query row per
+//              thread), dQ += dS.K with A from TMEM.
+// TMEM: [0,128) S or S^T, [128,256) dP or dP^T, then the d-column accumulators
+// (dV, dK or dQ). The 16-bit P / dS overwrite the first 64 columns of the score
+// block they come from, after the thread has read them.
+//
+// Warps: 0-3 elementwise (TMEM lane quarter w), 4 TMA producer, 5 TMEM allocator
+// and MMA issuer (one thread). Every wait is bounded (status word, abort flag).
+//
+// The depth part (each token's own L rows, read only by that token's G query
+// rows) is small: moda_bwd_depth_token_kernel stages one token's rows in shared
+// memory and writes dK_depth, dV_depth and adds the depth term of dQ.
+#include "moda_internal.h"
+
+#include <cstdio>
+
+namespace moda {
+
+namespace {
+
+constexpr int kBThreads = 192;
+constexpr int kBRows = 128;      // rows per tile (query rows or keys)
+constexpr int kWarpProd = 4, kWarpMma = 5;
+constexpr int MODE_DKDV = 0, MODE_DQ = 1;
+
+template <int HD>
+struct BwdCfg {
+    static constexpr int kTile = kBRows * HD * 2;          // one 128 x HD 16-bit tile
+    static constexpr int kColBlocks = HD / 64;
+    static constexpr int kStages = HD == 128 ? 2 : 4;      // ring of tile pairs
+    static constexpr int kResOff = 0;                       // resident pair
+    static constexpr int kRingOff = 2 * kTile;
+    static constexpr int kStageOff = kRingOff + kStages * 2 * kTile;   // lse/D staging
+    static constexpr int kBarOff = kStageOff + 2 * 2 * kBRows * 4;
+    // res_full res_empty st_full pd_full acc_done acc_free end stage, ring_full[S] ring_empty[S]
+    static constexpr int kNumBars = 8 + 2 * kStages;
+    static constexpr int kMiscOff = kBarOff + kNumBars * 8;
+    static constexpr int kSmem = kMiscOff + 32 + 1024;
+    static constexpr uint32_t kTmemCols = 512;
+    static constexpr uint32_t kAcc0 = 256, kAcc1 = 256 + HD;
+};
+
+}  // namespace
+
+static __device__ int moda_bwd_status = 0;
+
+MODA_DEV bool bwait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int site) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 255u) == 0) {
+            if (*abort_flag) return false;
+            if (clock64() - t0 > kWaitLimitCycles) {
+                *abort_flag = 1;
+                atomicCAS(&moda_bwd_status, 0, 0x200 | site);
+                return false;
+            }
+        }
+    }
+}
+
+struct BwdItem {
+    int b, hk;
+    int res0;    // first token (DQ: query tile) or first key (DKDV: key tile)
+    int first;   // first step index (DKDV: query tile, DQ: key tile)
+    int nsteps;
+};
+
+template <int MODE>
+MODA_DEV BwdItem bwd_item(const TcBwdParams& p, int item) {
+    BwdItem it;
+    const int bh = p.B * p.Hk;
+    const int pos = item / bh, r = item % bh;
+    it.b = r / p.Hk;
+    it.hk = r % p.Hk;
+    if (MODE == MODE_DKDV) {
+        const int kt = pos;                          // ascending: most query tiles first
+        it.res0 = kt * kBRows;
+        it.first = it.res0 / p.n_tok;                // first query tile with a token >= res0
+        it.nsteps = p.num_qtiles - it.first;
+    } else {
+        const int qt = p.num_qtiles - 1 - pos;       // descending: most key blocks first
+        it.res0 = qt * p.n_tok;
+        const int last_tok = min(p.T, it.res0 + p.n_tok) - 1;
+        it.first = 0;
+        it.nsteps = last_tok / kBRows + 1;
+    }
+    return it;
+}
+
+template <int HD, int FMT, int MODE>
+__global__ void __launch_bounds__(kBThreads, 1) moda_bwd_tc_kernel(const __grid_constant__ TcBwdParams p) {
+    using Cfg = BwdCfg<HD>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    const uint32_t sbase = smem_u32(smem);
+    const uint32_t sRes = sbase + Cfg::kResOff;
+    const uint32_t sRing = sbase + Cfg::kRingOff;
+    const uint32_t bar0 = sbase + Cfg::kBarOff;
+    const uint32_t res_full = bar0, res_empty = bar0 + 8, st_full = bar0 + 16, pd_full = bar0 + 24;
+    const uint32_t acc_done = bar0 + 32, acc_free = bar0 + 40, end_bar = bar0 + 48;
+    // DKDV: the four elementwise warps have staged their rows' lse and D for a step
+    const uint32_t stage_bar = bar0 + 56;
+    auto ring_full = [&](uint32_t i) { return bar0 + 8u * (8 + i); };
+    auto ring_empty = [&](uint32_t i) { return bar0 + 8u * (8 + Cfg::kStages + i); };
+    float* stage = reinterpret_cast<float*>(smem + Cfg::kStageOff);  // [2][2][128]: lse2, D
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + Cfg::kMiscOff);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Cfg::kMiscOff + 8);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    constexpr uint32_t kTile = Cfg::kTile;
+
+    if (threadIdx.x == 0) {
+        mbar_init(res_full, 1);
+        mbar_init(res_empty, 1);
+        mbar_init(st_full, 1);
+        mbar_init(pd_full, 4);
+        mbar_init(acc_done, 1);
+        mbar_init(acc_free, 4);
+        mbar_init(end_bar, 1);
+        mbar_init(stage_bar, 4);
+        for (int i = 0; i < Cfg::kStages; ++i) {
+            mbar_init(ring_full(i), 1);
+            mbar_init(ring_empty(i), 1);
+        }
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == kWarpMma) {
+        tmem_alloc(smem_u32(tmem_holder), Cfg::kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_holder;
+    // resident pair: DKDV (K, V) key tile, DQ (Q, dO) query tile; ring pairs the other way
+    const CUtensorMap* res_m0 = MODE == MODE_DKDV ? &p.tm_k : &p.tm_q;
+    const CUtensorMap* res_m1 = MODE == MODE_DKDV ? &p.tm_v : &p.tm_do;
+    const CUtensorMap* ring_m0 = MODE == MODE_DKDV ? &p.tm_q : &p.tm_k;
+    const CUtensorMap* ring_m1 = MODE == MODE_DKDV ? &p.tm_do : &p.tm_v;
+
+    if (warp == kWarpProd) {
+        if (lane == 0) {
+            // ------------------------------------------------------------ TMA producer
+            uint32_t f = 0, nres = 0;
+            bool ok = true;
+            // coordinates of a tile: key-like (d, row, hk, b), query-like (d, hk*G, tok, b)
+            auto load_pair = [&](const CUtensorMap* m0, const CUtensorMap* m1, bool keylike, int row0,
+                                 const BwdItem& it, uint32_t dst, uint32_t bar) {
+                mbar_expect_tx(bar, 2 * kTile);
+                for (int cb = 0; cb < Cfg::kColBlocks; ++cb) {
+                    if (keylike) {
+                        tma_load_4d(m0, dst + cb * 16384, bar, cb * 64, row0, it.hk, it.b);
+                        tma_load_4d(m1, dst + kTile + cb * 16384, bar, cb * 64, row0, it.hk, it.b);
+                    } else {
+                        tma_load_4d(m0, dst + cb * 16384, bar, cb * 64, it.hk * p.G, row0, it.b);
+                        tma_load_4d(m1, dst + kTile + cb * 16384, bar, cb * 64, it.hk * p.G, row0, it.b);
+                    }
+                }
+            };
+            for (int item = blockIdx.x; item < p.num_items && ok; item += gridDim.x) {
+                const BwdItem it = bwd_item<MODE>(p, item);
+                ok = bwait(res_empty, (nres & 1u) ^ 1u, abort_flag, 1);
+                if (!ok) break;
+                load_pair(res_m0, res_m1, MODE == MODE_DKDV, it.res0, it, sRes, res_full);
+                ++nres;
+                for (int s = 0; s < it.nsteps && ok; ++s) {
+                    const uint32_t slot = f % Cfg::kStages;
+                    ok = bwait(ring_empty(slot), ((f / Cfg::kStages) & 1u) ^ 1u, abort_flag, 2);
+                    if (!ok) break;
+                    const int idx = it.first + s;
+                    if (MODE == MODE_DKDV)
+                        load_pair(ring_m0, ring_m1, false, idx * p.n_tok, it, sRing + slot * 2 * kTile,
+                                  ring_full(slot));
+                    else
+                        load_pair(ring_m0, ring_m1, true, idx * kBRows, it, sRing + slot * 2 * kTile,
+                                  ring_full(slot));
+                    ++f;
+                }
+            }
+            // exit: loads in flight must land before shared memory goes away
+            const uint32_t lo = f > Cfg::kStages ? f - Cfg::kStages : 0;
+            for (uint32_t fi = lo; fi < f; ++fi)
+                mbar_wait_drain(ring_full(fi % Cfg::kStages), (fi / Cfg::kStages) & 1u);
+            if (nres > 0) mbar_wait_drain(res_full, (nres - 1) & 1u);
+        }
+    } else if (warp == kWarpMma) {
+        if (lane == 0) {
+            // ------------------------------------------------------------ MMA issuer
+            constexpr uint32_t idesc_s = make_idesc(FMT, kBRows, kBRows, 0);  // B K-major (d)
+            constexpr uint32_t idesc_o = make_idesc(FMT, kBRows, HD, 1);      // B MN-major (d)
+            constexpr uint32_t hi = desc_hi_sw128(1024);
+            const uint32_t a0 = desc_lo(sRes, 16), a1 = desc_lo(sRes + kTile, 16);
+            const uint32_t tS = tmem, tP = tmem + 128;
+            uint32_t f = 0, nres = 0, nst = 0, nitems = 0;
+            bool ok = true;
+            for (int item = blockIdx.x; item < p.num_items && ok; item += gridDim.x) {
+                const BwdItem it = bwd_item<MODE>(p, item);
+                ok = bwait(res_full, nres & 1u, abort_flag, 3);
+                if (!ok) break;
+                ++nres;
+                for (int s = 0; s < it.nsteps; ++s) {
+                    const uint32_t slot = f % Cfg::kStages;
+                    const uint32_t rb = sRing + slot * 2 * kTile;
+                    ok = bwait(ring_full(slot), (f / Cfg::kStages) & 1u, abort_flag, 4);
+                    if (!ok) break;
+                    tc_fence_after();
+                    // S (S^T) = res0 . ring0^T and dP (dP^T) = res1 . ring1^T, contraction over d
+                    const uint32_t b0 = desc_lo(rb, 16), b1 = desc_lo(rb + kTile, 16);
+#pragma unroll
+                    for (int kk = 0; kk < HD / 16; ++kk) {
+                        const uint32_t off = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
+                        mma_ss(tS, desc_join(a0 + off, hi), desc_join(b0 + off, hi), idesc_s, kk > 0);
+                    }
+#pragma unroll
+                    for (int kk = 0; kk < HD / 16; ++kk) {
+                        const uint32_t off = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
+                        mma_ss(tP, desc_join(a1 + off, hi), desc_join(b1 + off, hi), idesc_s, kk > 0);
+                    }
+                    mma_commit(st_full);
+                    if (s == it.nsteps - 1) mma_commit(res_empty);  // resident tiles no longer read
+                    ok = bwait(pd_full, nst & 1u, abort_flag, 5);
+                    ++nst;
+                    if (ok && s == 0 && nitems > 0) ok = bwait(acc_free, (nitems - 1) & 1u, abort_flag, 6);
+                    if (!ok) break;
+                    tc_fence_after();
+                    // contraction over the 128 rows of the ring tiles (MN-major B, d contiguous)
+                    const uint32_t v0 = desc_lo(rb, 16384), v1 = desc_lo(rb + kTile, 16384);
+                    if (MODE == MODE_DKDV) {
+#pragma unroll
+                        for (int kk = 0; kk < kBRows / 16; ++kk)   // dV += P^T . dO
+                            mma_ts(tmem + Cfg::kAcc0, tS + kk * 8, desc_join(v1 + ((kk * 2048) >> 4), hi),
+                                   idesc_o, (s == 0 && kk == 0) ? 0u : 1u);
+#pragma unroll
+                        for (int kk = 0; kk < kBRows / 16; ++kk)   // dK += dS^T . Q
+                            mma_ts(tmem + Cfg::kAcc1, tP + kk * 8, desc_join(v0 + ((kk * 2048) >> 4), hi),
+                                   idesc_o, (s == 0 && kk == 0) ? 0u : 1u);
+                    } else {
+#pragma unroll
+                        for (int kk = 0; kk < kBRows / 16; ++kk)   // dQ += dS . K
+                            mma_ts(tmem + Cfg::kAcc0, tS + kk * 8, desc_join(v0 + ((kk * 2048) >> 4), hi),
+                                   idesc_o, (s == 0 && kk == 0) ? 0u : 1u);
+                    }
+                    mma_commit(ring_empty(slot));
+                    if (s == it.nsteps - 1) mma_commit(acc_done);
+                    ++f;
+                }
+                ++nitems;
+            }
+            mma_commit(end_bar);
+            mbar_wait_drain(end_bar, 0);
+        }
+    } else {
+        // ------------------------------------------------------------ elementwise warps
+        const int wq = warp;  // TMEM lane quarter
+        const int row = wq * 32 + lane;
+        const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+        const uint32_t tS = tmem + lane_off, tP = tmem + lane_off + 128;
+        const float sc2 = p.sc;
+        const int gsh = __ffs(p.G) - 1;  // G divides 128: a power of two
+        uint32_t nst = 0, nitems = 0;
+        bool ok = true;
+        for (int item = blockIdx.x; item < p.num_items && ok; item += gridDim.x) {
+            const BwdItem it = bwd_item<MODE>(p, item);
+            // DQ: this thread's query row; its lse and D stay in registers
+            int tok_r = 0;
+            float lse2_r = INFINITY, D_r = 0.f;
+            if (MODE == MODE_DQ) {
+                tok_r = it.res0 + (row >> gsh);
+                if (tok_r < p.T) {
+                    const long long ri = (static_cast<long long>(it.b) * p.Hq + it.hk * p.G + (row & (p.G - 1))) * p.T + tok_r;
+                    lse2_r = p.lse[ri] * kLog2e;
+                    D_r = p.delta[ri];
+                }
+            }
+            const int key_r = it.res0 + row;  // DKDV: this thread's key
+            for (int s = 0; s < it.nsteps; ++s) {
+                const int idx = it.first + s;
+                float* st_lse = stage + (nst & 1u) * 256;
+                float* st_D = st_lse + 128;
+                int col0;       // DKDV: first query token of the tile; DQ: first key of the block
+                bool need_mask;
+                if (MODE == MODE_DKDV) {
+                    col0 = idx * p.n_tok;
+                    // stage lse and D of the tile's 128 query rows (column q <-> token q/G, head q%G)
+                    const int tq = col0 + (row >> gsh);
+                    float l2 = INFINITY, dd = 0.f;
+                    if (tq < p.T) {
+                        const long long ri = (static_cast<long long>(it.b) * p.Hq + it.hk * p.G + (row & (p.G - 1))) * p.T + tq;
+                        l2 = p.lse[ri] * kLog2e;
+                        dd = p.delta[ri];
+                    }
+                    st_lse[row] = l2;
+                    st_D[row] = dd;
+                    // all four warps staged (one phase per step; a warp reaches the next
+                    // phase only after every warp arrived, so parities never alias)
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(stage_bar);
+                    if (!bwait(stage_bar, nst & 1u, abort_flag, 9)) { ok = false; break; }
+                    need_mask = col0 < it.res0 + kBRows;   // some token of the tile below some key
+                } else {
+                    col0 = idx * kBRows;
+                    need_mask = col0 + kBRows - 1 > it.res0;  // some key above some token
+                }
+                if (!bwait(st_full, nst & 1u, abort_flag, 7)) { ok = false; break; }
+                tc_fence_after();
+#pragma unroll 1
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t sv[32], dv[32];
+                    tmem_ld32(tS + 32 * c, sv);
+                    tmem_ld32(tP + 32 * c, dv);
+                    tmem_wait_ld();
+                    tmem_reg_fence(sv);
+                    tmem_reg_fence(dv);
+                    uint32_t pk_p[16], pk_d[16];
+#pragma unroll
+                    for (int i = 0; i < 32; i += 2) {
+                        float pr[2], ds[2];
+#pragma unroll
+                        for (int u = 0; u < 2; ++u) {
+                            const int col = 32 * c + i + u;
+                            float l2, dd;
+                            bool valid;
+                            if (MODE == MODE_DKDV) {
+                                l2 = st_lse[col];
+                                dd = st_D[col];
+                                valid = !need_mask || col0 + (col >> gsh) >= key_r;
+                            } else {
+                                l2 = lse2_r;
+                                dd = D_r;
+                                valid = !need_mask || col0 + col <= tok_r;
+                            }
+                            const float e = ex2(fmaf(__uint_as_float(sv[i + u]), sc2, -l2));
+                            pr[u] = valid ? e : 0.f;
+                            ds[u] = pr[u] * (__uint_as_float(dv[i + u]) - dd);
+                        }
+                        pk_p[i >> 1] = FMT == 1 ? pack_bf16x2(pr[0], pr[1]) : pack_f16x2(pr[0], pr[1]);
+                        pk_d[i >> 1] = FMT == 1 ? pack_bf16x2(ds[0], ds[1]) : pack_f16x2(ds[0], ds[1]);
+                    }
+                    // 16-bit results go into columns this thread has already read
+                    if (MODE == MODE_DKDV) {
+                        tmem_st16(tS + 16 * c, pk_p);   // P^T
+                        tmem_st16(tP + 16 * c, pk_d);   // dS^T
+                    } else {
+                        tmem_st16(tS + 16 * c, pk_d);   // dS
+                    }
+                }
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(pd_full);
+                ++nst;
+            }
+            if (!ok) break;
+            // ------------------------------------------------------------ epilogue
+            if (!bwait(acc_done, nitems & 1u, abort_flag, 8)) { ok = false; break; }
+            ++nitems;
+            tc_fence_after();
+            uint4* dst0;
+            uint4* dst1 = nullptr;
+            bool valid;
+            if (MODE == MODE_DKDV) {
+                valid = key_r < p.T;
+                dst0 = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.dv) + it.b * p.dv_sb + it.hk * p.dv_sh +
+                                                static_cast<long long>(key_r) * p.dv_st);
+                dst1 = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.dk) + it.b * p.dk_sb + it.hk * p.dk_sh +
+                                                static_cast<long long>(key_r) * p.dk_st);
+            } else {
+                valid = tok_r < p.T;
+                const int head = it.hk * p.G + (row & (p.G - 1));
+                dst0 = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.dq) + it.b * p.dq_sb + head * p.dq_sh +
+                                                static_cast<long long>(tok_r) * p.dq_st);
+            }
+#pragma unroll
+            for (int a = 0; a < (MODE == MODE_DKDV ? 2 : 1); ++a) {
+                const uint32_t tacc = tmem + lane_off + (a == 0 ? Cfg::kAcc0 : Cfg::kAcc1);
+                // dV is P^T.dO as is; dK and dQ carry the softmax scale
+                const float mul = (MODE == MODE_DKDV && a == 0) ? 1.f : p.scale;
+                uint4* dst = a == 0 ? dst0 : dst1;
+#pragma unroll
+                for (int cb = 0; cb < HD; cb += 32) {
+                    uint32_t ov[32];
+                    tmem_ld32_sync(tacc + cb, ov);
+                    uint32_t pk[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const float x0 = __uint_as_float(ov[2 * i]) * mul, x1 = __uint_as_float(ov[2 * i + 1]) * mul;
+                        pk[i] = FMT == 1 ? pack_bf16x2(x0, x1) : pack_f16x2(x0, x1);
+                    }
+                    if (valid) {
+#pragma unroll
+                        for (int ch = 0; ch < 4; ++ch)
+                            dst[(cb >> 3) + ch] = make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_free);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kWarpMma) {
+        tc_fence_after();
+        tmem_dealloc(tmem, Cfg::kTmemCols);
+    }
+}
+
+// ---------------------------------------------------------------- depth part
+namespace {
+template <typename T>
+MODA_DEV float ldf(const T* p);
+template <>
+MODA_DEV float ldf<__nv_bfloat16>(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+template <>
+MODA_DEV float ldf<__half>(const __half* p) { return __half2float(*p); }
+template <>
+MODA_DEV float ldf<float>(const float* p) { return *p; }
+template <typename T>
+MODA_DEV void stf(T* p, float x);
+template <>
+MODA_DEV void stf<__nv_bfloat16>(__nv_bfloat16* p, float x) { *p = __float2bfloat16_rn(x); }
+template <>
+MODA_DEV void stf<__half>(__half* p, float x) { *p = __float2half_rn(x); }
+template <>
+MODA_DEV void stf<float>(float* p, float x) { *p = x; }
+
+template <typename T>
+MODA_DEV T* rowp(const ModaTensor& t, int b, int h, long long r) {
+    return static_cast<T*>(t.ptr) + b * t.strides[0] + h * t.strides[1] + r * t.strides[2];
+}
+}  // namespace
+
+constexpr int kDepthChunk = 32;  // depth rows staged per pass
+
+// One block per token (b, KV head, t): its G query rows against its L depth rows
+// [t*L, (t+1)*L), in passes of kDepthChunk rows. Writes dK_depth, dV_depth for those
+// rows and adds scale * sum_l dS_l kd_l to the token's dQ rows (which the sequence
+// kernels wrote before this launch).
+template <typename T>
+__global__ void __launch_bounds__(128) moda_bwd_depth_token_kernel(const __grid_constant__ BwdParams p) {
+    extern __shared__ float sm[];
+    const int t = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
+    const int G = p.G, L = p.L, d = p.d, dp1 = d + 1;
+    const int LC = min(L, kDepthChunk);
+    float* s_kd = sm;                  // [LC][d+1]
+    float* s_vd = s_kd + LC * dp1;     // [LC][d+1]
+    float* s_q = s_vd + LC * dp1;      // [G][d+1]
+    float* s_do = s_q + G * dp1;       // [G][d+1]
+    float* s_dq = s_do + G * dp1;      // [G][d]
+    float* s_p = s_dq + G * d;         // [G][LC]
+    float* s_ds = s_p + G * LC;        // [G][LC]
+    float* s_lse = s_ds + G * LC;      // [G]
+    float* s_D = s_lse + G;            // [G]
+    const int tid = threadIdx.x, nth = blockDim.x;
+    const float sc2 = p.scale * kLog2e;
+    for (int i = tid; i < G * d; i += nth) {
+        const int g = i / d, e = i % d, h = hk * G + g;
+        s_q[g * dp1 + e] = ldf<T>(rowp<const T>(p.q, b, h, t) + e * p.q.strides[3]);
+        s_do[g * dp1 + e] = ldf<T>(rowp<const T>(p.dout, b, h, t) + e * p.dout.strides[3]);
+        s_dq[i] = 0.f;
+    }
+    for (int g = tid; g < G; g += nth) {
+        const long long ri = (static_cast<long long>(b) * p.Hq + hk * G + g) * p.T + t;
+        s_lse[g] = p.lse[ri] * kLog2e;
+        s_D[g] = p.delta[ri];
+    }
+    for (int l0 = 0; l0 < L; l0 += LC) {
+        const int nl = min(LC, L - l0);
+        const long long r0 = static_cast<long long>(t) * L + l0;
+        __syncthreads();  // previous pass done with the staged rows
+        for (int i = tid; i < nl * d; i += nth) {
+            const int l = i / d, e = i % d;
+            s_kd[l * dp1 + e] = ldf<T>(rowp<const T>(p.kd, b, hk, r0 + l) + e * p.kd.strides[3]);
+            s_vd[l * dp1 + e] = ldf<T>(rowp<const T>(p.vd, b, hk, r0 + l) + e * p.vd.strides[3]);
+        }
+        __syncthreads();
+        for (int i = tid; i < G * nl; i += nth) {
+            const int g = i / nl, l = i % nl;
+            float s = 0.f, dp = 0.f;
+            for (int e = 0; e < d; ++e) {
+                s = fmaf(s_q[g * dp1 + e], s_kd[l * dp1 + e], s);
+                dp = fmaf(s_do[g * dp1 + e], s_vd[l * dp1 + e], dp);
+            }
+            const float pr = ex2(fmaf(s, sc2, -s_lse[g]));
+            s_p[g * LC + l] = pr;
+            s_ds[g * LC + l] = pr * (dp - s_D[g]);
+        }
+        __syncthreads();
+        for (int i = tid; i < nl * d; i += nth) {
+            const int l = i / d, e = i % d;
+            float ak = 0.f, av = 0.f;
+            for (int g = 0; g < G; ++g) {
+                ak = fmaf(s_ds[g * LC + l], s_q[g * dp1 + e], ak);
+                av = fmaf(s_p[g * LC + l], s_do[g * dp1 + e], av);
+            }
+            stf<T>(rowp<T>(p.dkd, b, hk, r0 + l) + e * p.dkd.strides[3], ak * p.scale);
+            stf<T>(rowp<T>(p.dvd, b, hk, r0 + l) + e * p.dvd.strides[3], av);
+        }
+        for (int i = tid; i < G * d; i += nth) {
+            const int g = i / d, e = i % d;
+            float a = s_dq[i];
+            for (int l = 0; l < nl; ++l) a = fmaf(s_ds[g * LC + l], s_kd[l * dp1 + e], a);
+            s_dq[i] = a;
+        }
+    }
+    __syncthreads();
+    for (int i = tid; i < G * d; i += nth) {
+        const int g = i / d, e = i % d, h = hk * G + g;
+        T* dq = rowp<T>(p.dq, b, h, t) + e * p.dq.strides[3];
+        stf<T>(dq, ldf<T>(dq) + s_dq[i] * p.scale);
+    }
+}
+
+// Zero gradient for depth rows the forward never reads (rows >= T*L).
+template <typename T>
+__global__ void moda_bwd_zero_rows_kernel(const __grid_constant__ BwdParams p, long long r_lo) {
+    const long long r = r_lo + blockIdx.x;
+    const int hk = blockIdx.y, b = blockIdx.z;
+    for (int e = threadIdx.x; e < p.d; e += blockDim.x) {
+        stf<T>(rowp<T>(p.dkd, b, hk, r) + e * p.dkd.strides[3], 0.f);
+        stf<T>(rowp<T>(p.dvd, b, hk, r) + e * p.dvd.strides[3], 0.f);
+    }
+}
+
+size_t depth_token_smem(int G, int L, int d) {
+    const int LC = L < kDepthChunk ? L : kDepthChunk;
+    return sizeof(float) * (static_cast<size_t>(2 * LC + 2 * G) * (d + 1) + static_cast<size_t>(G) * d +
+                            2 * static_cast<size_t>(G) * LC + 2 * static_cast<size_t>(G));
+}
+
+template <typename T>
+static int launch_depth_t(const BwdParams& p, cudaStream_t stream) {
+    if (p.L > 0 && p.T > 0) {
+        const size_t sm = depth_token_smem(p.G, p.L, p.d);
+        if (sm > 48 * 1024 &&
+            cudaFuncSetAttribute(moda_bwd_depth_token_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(sm)) != cudaSuccess)
+            return MODA_ERR_LAUNCH;
+        moda_bwd_depth_token_kernel<T><<<dim3(p.T, p.Hk, p.B), 128, sm, stream>>>(p);
+    }
+    const long long used = static_cast<long long>(p.T) * p.L;
+    if (p.R > used)
+        moda_bwd_zero_rows_kernel<T><<<dim3(static_cast<unsigned>(p.R - used), p.Hk, p.B), 64, 0, stream>>>(p, used);
+    return MODA_OK;
+}
+
+int launch_bwd_depth(const BwdParams& p, cudaStream_t stream) {
+    switch (p.dtype) {
+        case MODA_F32: return launch_depth_t<float>(p, stream);
+        case MODA_BF16: return launch_depth_t<__nv_bfloat16>(p, stream);
+        case MODA_F16: return launch_depth_t<__half>(p, stream);
+        default: return MODA_ERR_DTYPE;
+    }
+}
+
+bool bwd_depth_supported(const BwdParams& p) {
+    return depth_token_smem(p.G, p.L, p.d) <= 200 * 1024 && p.R - static_cast<long long>(p.T) * p.L < (1LL << 31);
+}
+
+// ---------------------------------------------------------------- host side
+bool tc_bwd_supports(const BwdParams& p, char* why, size_t whylen) {
+    auto no = [&](const char* m) {
+        snprintf(why, whylen, "%s", m);
+        return false;
+    };
+    if (p.dtype != MODA_BF16 && p.dtype != MODA_F16) return no("tcgen05 backward needs bf16 or f16");
+    if (p.d != 64 && p.d != 128) return no("tcgen05 backward needs head_dim 64 or 128");
+    if (p.G < 1 || (128 % p.G) != 0) return no("tcgen05 backward needs H_q/H_k dividing 128");
+    if (!bwd_depth_supported(p)) return no("depth part too large for the per-token kernel");
+    if (!(p.scale > 0.f)) return no("tcgen05 backward needs a positive scale");
+    const ModaTensor* ts[7] = {&p.q, &p.k, &p.v, &p.dout, &p.dq, &p.dk, &p.dv};
+    for (const ModaTensor* t : ts) {
+        if (t->strides[3] != 1) return no("tcgen05 backward needs unit stride along head_dim");
+        if (reinterpret_cast<uintptr_t>(t->ptr) % 16 != 0) return no("tcgen05 backward needs 16-byte aligned tensors");
+        for (int i = 0; i < 3; ++i)
+            if (t->sizes[i] > 1 && (t->strides[i] * 2) % 16 != 0)
+                return no("tcgen05 backward needs 16-byte multiple strides");
+    }
+    return true;
+}
+
+cudaError_t read_and_clear_bwd_status(cudaStream_t stream, int* value) {
+    cudaError_t e = cudaMemcpyFromSymbolAsync(value, moda_bwd_status, sizeof(int), 0,
+                                              cudaMemcpyDeviceToHost, stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    if (e == cudaSuccess && *value != 0) {
+        static const int zero = 0;
+        e = cudaMemcpyToSymbolAsync(moda_bwd_status, &zero, sizeof(int), 0, cudaMemcpyHostToDevice,
+                                    stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    }
+    return e;
+}
+
+template <int HD, int FMT, int MODE>
+static int launch_bwd_inst(const TcBwdParams& tp, int items, cudaStream_t stream) {
+    using Cfg = BwdCfg<HD>;
+    auto kern = moda_bwd_tc_kernel<HD, FMT, MODE>;
+    static bool attr_set = false;
+    if (!attr_set) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem) != cudaSuccess)
+            return MODA_ERR_LAUNCH;
+        attr_set = true;
+    }
+    if (items == 0) return MODA_OK;
+    const int grid = items < sm_count() ? items : sm_count();
+    kern<<<grid, kBThreads, Cfg::kSmem, stream>>>(tp);
+    return MODA_OK;
+}
+
+template <int HD, int FMT>
+static int launch_bwd_pair(TcBwdParams& tp, cudaStream_t stream) {
+    const int bh = tp.B * tp.Hk;
+    tp.num_items = tp.num_ktiles * bh;
+    int r = launch_bwd_inst<HD, FMT, MODE_DKDV>(tp, tp.num_items, stream);
+    if (r != MODA_OK) return r;
+    tp.num_items = tp.num_qtiles * bh;
+    return launch_bwd_inst<HD, FMT, MODE_DQ>(tp, tp.num_items, stream);
+}
+
+int launch_bwd_tc(const BwdParams& p, cudaStream_t stream, char* err, size_t errlen) {
+    TcBwdParams tp;
+    const CUtensorMapDataType dt =
+        p.dtype == MODA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const int n_tok = 128 / p.G;
+    if (!encode_map(&tp.tm_q, p.q, p.T, true, 2, dt, p.G, n_tok, err, errlen, "Q") ||
+        !encode_map(&tp.tm_do, p.dout, p.T, true, 2, dt, p.G, n_tok, err, errlen, "dO") ||
+        !encode_map(&tp.tm_k, p.k, p.T, false, 2, dt, kBRows, 1, err, errlen, "K") ||
+        !encode_map(&tp.tm_v, p.v, p.T, false, 2, dt, kBRows, 1, err, errlen, "V"))
+        return MODA_ERR_LAUNCH;
+    tp.lse = p.lse;
+    tp.delta = p.delta;
+    tp.dq = p.dq.ptr;
+    tp.dq_sb = p.dq.strides[0]; tp.dq_sh = p.dq.strides[1]; tp.dq_st = p.dq.strides[2];
+    tp.dk = p.dk.ptr;
+    tp.dk_sb = p.dk.strides[0]; tp.dk_sh = p.dk.strides[1]; tp.dk_st = p.dk.strides[2];
+    tp.dv = p.dv.ptr;
+    tp.dv_sb = p.dv.strides[0]; tp.dv_sh = p.dv.strides[1]; tp.dv_st = p.dv.strides[2];
+    tp.B = p.B; tp.Hq = p.Hq; tp.Hk = p.Hk; tp.G = p.G; tp.T = p.T;
+    tp.n_tok = n_tok;
+    tp.num_qtiles = (p.T + n_tok - 1) / n_tok;
+    tp.num_ktiles = (p.T + kBRows - 1) / kBRows;
+    tp.sc = p.scale * kLog2e;
+    tp.scale = p.scale;
+    const long long items = static_cast<long long>(tp.num_qtiles) * p.B * p.Hk;
+    if (items > 0x7fffffffLL) {
+        snprintf(err, errlen, "too many work items");
+        return MODA_ERR_UNSUPPORTED;
+    }
+    if (p.d == 128)
+        return p.dtype == MODA_BF16 ? launch_bwd_pair<128, 1>(tp, stream) : launch_bwd_pair<128, 0>(tp, stream);
+    return p.dtype == MODA_BF16 ? launch_bwd_pair<64, 1>(tp, stream) : launch_bwd_pair<64, 0>(tp, stream);
+}
+
+}  // namespace moda

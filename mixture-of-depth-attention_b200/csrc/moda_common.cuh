@@ -263,6 +263,20 @@ MODA_DEV void mma_commit(uint32_t bar) {
 }
 
 MODA_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Emits nothing. The registers of a tcgen05.ld are valid only after tcgen05.wait::ld;
+// passing them through this volatile asm (ordered after the wait) makes every later
+// use depend on a definition that follows the wait, so no computation on them can be
+// scheduled before it.
+MODA_DEV void tmem_reg_fence(uint32_t (&r)[32]) {
+    asm volatile(""
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                   "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                   "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]),
+                   "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
+                   "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]),
+                   "+r"(r[30]), "+r"(r[31]));
+}
 MODA_DEV void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // 32 lanes x 32 consecutive 32-bit columns; thread i <-> lane (base lane + i).
@@ -277,6 +291,13 @@ MODA_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
           "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
         : "r"(taddr)
         : "memory");
+}
+
+// tcgen05.ld of 32 columns followed by the wait and the register fence.
+MODA_DEV void tmem_ld32_sync(uint32_t taddr, uint32_t (&r)[32]) {
+    tmem_ld32(taddr, r);
+    tmem_wait_ld();
+    tmem_reg_fence(r);
 }
 
 MODA_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {

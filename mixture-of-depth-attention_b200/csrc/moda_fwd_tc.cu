@@ -716,7 +716,7 @@ static cuuint64_t tma_stride(int64_t size, int64_t stride_elems, int esz) {
 
 // Map over a [B, H, rows, d] view with dimension order (d, a, c, B) where a/c are
 // either (rows, H) for key-like tensors or (H, rows) for query-like tensors.
-static bool encode_map(CUtensorMap* m, const ModaTensor& t, int rows, bool head_inner, int esz,
+bool encode_map(CUtensorMap* m, const ModaTensor& t, int rows, bool head_inner, int esz,
                        CUtensorMapDataType dt, uint32_t box1, uint32_t box2, char* err,
                        size_t errlen, const char* name) {
     EncodeTiledFn enc = get_encode_fn();
@@ -809,7 +809,7 @@ static int launch_tc_inst(const TcParams& tp, int grid, cudaStream_t stream) {
     return MODA_OK;
 }
 
-static int sm_count() {
+int sm_count() {
     int dev = 0, n = 0;
     if (cudaGetDevice(&dev) != cudaSuccess ||
         cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)

@@ -46,11 +46,43 @@ struct TcParams {
     float* lse;     // optional [B, H_q, T] fp32 log-sum-exp output
 };
 
+// TMA map over a [B, H, rows, d] view (128-byte swizzle, box (64, box1, box2, 1)),
+// dimension order (d, H, rows, B) when head_inner (query-like tensors: box (64, G, n)
+// is a token-major tile of G heads x n tokens), else (d, rows, H, B).
+bool encode_map(CUtensorMap* m, const ModaTensor& t, int rows, bool head_inner, int esz,
+                CUtensorMapDataType dt, uint32_t box1, uint32_t box2, char* err, size_t errlen,
+                const char* name);
+int sm_count();
+
 int launch_fwd_simt(const FwdParams& p, cudaStream_t stream);
 int launch_fwd_tc(const FwdParams& p, cudaStream_t stream, char* err, size_t errlen);
 bool tc_supports(const FwdParams& p, char* why, size_t whylen);
 int launch_depth_append(const AppendParams& p, bool vec16, cudaStream_t stream);
-int launch_bwd(const BwdParams& p, cudaStream_t stream);
+// Parameters of the tcgen05 backward kernels. Tensor maps first (64-byte aligned).
+struct TcBwdParams {
+    CUtensorMap tm_q, tm_do, tm_k, tm_v;
+    const float* lse;
+    const float* delta;
+    void* dq;
+    long long dq_sb, dq_sh, dq_st;
+    void* dk;
+    long long dk_sb, dk_sh, dk_st;
+    void* dv;
+    long long dv_sb, dv_sh, dv_st;
+    int B, Hq, Hk, G, T;
+    int n_tok;       // tokens per 128-row query tile (128 / G)
+    int num_qtiles;  // query tiles per (b, kv head)
+    int num_ktiles;  // 128-key tiles per (b, kv head)
+    int num_items;
+    float sc;        // scale * log2(e)
+    float scale;
+};
+
+int launch_bwd(const BwdParams& p, cudaStream_t stream, char* err, size_t errlen);
+bool tc_bwd_supports(const BwdParams& p, char* why, size_t whylen);
+int launch_bwd_tc(const BwdParams& p, cudaStream_t stream, char* err, size_t errlen);
+int launch_bwd_depth(const BwdParams& p, cudaStream_t stream);
+cudaError_t read_and_clear_bwd_status(cudaStream_t stream, int* value);
 constexpr int kMaxDevices = 64;
 // Device address of the library's fixed backward scratch on the current device.
 cudaError_t noalloc_scratch(void** ptr);

@@ -115,6 +115,9 @@ def moda_backward(dO: Tensor, Q: Tensor, K: Tensor, V: Tensor, K_depth: Tensor,
             raise _lib.MoDAShapeError(f"{n} must have Q's shape, dtype and device")
     if lse.dtype != torch.float32 or lse.shape != Q.shape[:3] or not lse.is_contiguous():
         raise _lib.MoDAShapeError("lse must be a contiguous float32 [B, H_q, T] tensor")
+    # autograd may hand over an expanded (zero-stride) dO; the tensor-core path loads
+    # it with TMA, which needs real 16-byte strides
+    dO = dO.contiguous()
     grads = [torch.empty(t.shape, dtype=t.dtype, device=t.device) for t in (Q, K, V, K_depth, V_depth)]
     lib = _lib.load()
     nbytes = lib.moda_bwd_workspace_size(Q.shape[0], Q.shape[1], Q.shape[2])
