@@ -534,6 +534,193 @@ __global__ void __launch_bounds__(128) moda_bwd_depth_token_kernel(const __grid_
     }
 }
 
+// One warp per token (b, KV head, t); lane l owns depth rows t*L + l + 32j (j < J).
+// The token's G query rows and dO rows are staged once in the warp's shared memory
+// (fp32); each lane reads its own depth rows with 16-byte loads. Per lane:
+//   s[j][g] = q_g . kd_r, dp[j][g] = dO_g . vd_r        (2*G*d FMA per row)
+//   dK_depth[r] = scale * sum_g dS q_g, dV_depth[r] = sum_g P dO_g
+// and the dQ term scale * sum_l dS_{g,l} kd_l goes through a shared-memory copy of
+// dS (lanes then split d). No block-wide synchronisation.
+constexpr int kDepthWarps = 4;
+
+template <typename T, int HD, int G, int J>
+__global__ void __launch_bounds__(kDepthWarps * 32) moda_bwd_depth_warp_kernel(const __grid_constant__ BwdParams p) {
+    static_assert(sizeof(T) == 2, "16-bit inputs");
+    __shared__ __align__(16) float s_q[kDepthWarps][G][HD];
+    __shared__ __align__(16) float s_do[kDepthWarps][G][HD];
+    __shared__ float s_ds[kDepthWarps][G][32 * J];
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long long tok_id = static_cast<long long>(blockIdx.x) * kDepthWarps + w;
+    if (tok_id >= static_cast<long long>(p.B) * p.Hk * p.T) return;
+    const int t = static_cast<int>(tok_id % p.T);
+    const int hk = static_cast<int>((tok_id / p.T) % p.Hk);
+    const int b = static_cast<int>(tok_id / (static_cast<long long>(p.T) * p.Hk));
+    const int L = p.L;
+    const float sc2 = p.scale * kLog2e;
+    // stage q and dO rows of the G heads (lanes split d, 8 elements per 16-byte load)
+    for (int i = lane; i < G * HD / 8; i += 32) {
+        const int g = i / (HD / 8), e = (i % (HD / 8)) * 8, h = hk * G + g;
+        const uint4 uq = *reinterpret_cast<const uint4*>(rowp<const T>(p.q, b, h, t) + e);
+        const uint4 ug = *reinterpret_cast<const uint4*>(rowp<const T>(p.dout, b, h, t) + e);
+        const T* tq = reinterpret_cast<const T*>(&uq);
+        const T* tg = reinterpret_cast<const T*>(&ug);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            s_q[w][g][e + k] = ldf<T>(tq + k);
+            s_do[w][g][e + k] = ldf<T>(tg + k);
+        }
+    }
+    float lse2[G], dlt[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        const long long ri = (static_cast<long long>(b) * p.Hq + hk * G + g) * p.T + t;
+        lse2[g] = p.lse[ri] * kLog2e;
+        dlt[g] = p.delta[ri];
+    }
+    __syncwarp();
+    const long long r0 = static_cast<long long>(t) * L;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+        const int l = lane + 32 * j;
+        float s[G], dp[G];
+#pragma unroll
+        for (int g = 0; g < G; ++g) s[g] = dp[g] = 0.f;
+        if (l < L) {
+            const T* kr = rowp<const T>(p.kd, b, hk, r0 + l);
+            const T* vr = rowp<const T>(p.vd, b, hk, r0 + l);
+#pragma unroll 4
+            for (int e = 0; e < HD; e += 8) {
+                const uint4 uk = *reinterpret_cast<const uint4*>(kr + e);
+                const uint4 uv = *reinterpret_cast<const uint4*>(vr + e);
+                const T* tk = reinterpret_cast<const T*>(&uk);
+                const T* tv = reinterpret_cast<const T*>(&uv);
+                float kf[8], vf[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    kf[k] = ldf<T>(tk + k);
+                    vf[k] = ldf<T>(tv + k);
+                }
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    const float4 q0 = *reinterpret_cast<const float4*>(&s_q[w][g][e]);
+                    const float4 q1 = *reinterpret_cast<const float4*>(&s_q[w][g][e + 4]);
+                    const float4 g0 = *reinterpret_cast<const float4*>(&s_do[w][g][e]);
+                    const float4 g1 = *reinterpret_cast<const float4*>(&s_do[w][g][e + 4]);
+                    s[g] = fmaf(q0.x, kf[0], fmaf(q0.y, kf[1], fmaf(q0.z, kf[2], fmaf(q0.w, kf[3], s[g]))));
+                    s[g] = fmaf(q1.x, kf[4], fmaf(q1.y, kf[5], fmaf(q1.z, kf[6], fmaf(q1.w, kf[7], s[g]))));
+                    dp[g] = fmaf(g0.x, vf[0], fmaf(g0.y, vf[1], fmaf(g0.z, vf[2], fmaf(g0.w, vf[3], dp[g]))));
+                    dp[g] = fmaf(g1.x, vf[4], fmaf(g1.y, vf[5], fmaf(g1.z, vf[6], fmaf(g1.w, vf[7], dp[g]))));
+                }
+            }
+        }
+        float pr[G], ds[G];
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            pr[g] = l < L ? ex2(fmaf(s[g], sc2, -lse2[g])) : 0.f;
+            ds[g] = pr[g] * (dp[g] - dlt[g]);
+            s_ds[w][g][l] = ds[g];
+        }
+        if (l < L) {
+            T* dkr = rowp<T>(p.dkd, b, hk, r0 + l);
+            T* dvr = rowp<T>(p.dvd, b, hk, r0 + l);
+#pragma unroll 2
+            for (int e = 0; e < HD; e += 8) {
+                float ak[8], av[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) ak[k] = av[k] = 0.f;
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        ak[k] = fmaf(ds[g], s_q[w][g][e + k], ak[k]);
+                        av[k] = fmaf(pr[g], s_do[w][g][e + k], av[k]);
+                    }
+                }
+                uint4 ok, ov;
+                T* tk = reinterpret_cast<T*>(&ok);
+                T* tv = reinterpret_cast<T*>(&ov);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    stf<T>(tk + k, ak[k] * p.scale);
+                    stf<T>(tv + k, av[k]);
+                }
+                *reinterpret_cast<uint4*>(dkr + e) = ok;
+                *reinterpret_cast<uint4*>(dvr + e) = ov;
+            }
+        }
+    }
+    __syncwarp();
+    // dQ_g[e] += scale * sum_l dS_{g,l} kd_l[e]: lanes split d (HD/32 elements each)
+    constexpr int EPL = HD / 32;
+    float acc[G][EPL];
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int k = 0; k < EPL; ++k) acc[g][k] = 0.f;
+    for (int l = 0; l < L; ++l) {
+        const T* kr = rowp<const T>(p.kd, b, hk, r0 + l) + lane * EPL;
+        float kf[EPL];
+        if constexpr (EPL == 4) {
+            const uint2 u = *reinterpret_cast<const uint2*>(kr);
+            const T* tk = reinterpret_cast<const T*>(&u);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) kf[k] = ldf<T>(tk + k);
+        } else {
+            const uint32_t u = *reinterpret_cast<const uint32_t*>(kr);
+            const T* tk = reinterpret_cast<const T*>(&u);
+#pragma unroll
+            for (int k = 0; k < EPL; ++k) kf[k] = ldf<T>(tk + k);
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const float dsv = s_ds[w][g][l];
+#pragma unroll
+            for (int k = 0; k < EPL; ++k) acc[g][k] = fmaf(dsv, kf[k], acc[g][k]);
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        T* dq = rowp<T>(p.dq, b, hk * G + g, t) + lane * EPL;
+#pragma unroll
+        for (int k = 0; k < EPL; ++k) stf<T>(dq + k, ldf<T>(dq + k) + acc[g][k] * p.scale);
+    }
+}
+
+template <typename T, int HD>
+static bool launch_depth_warp_hd(const BwdParams& p, cudaStream_t stream) {
+    const long long n = static_cast<long long>(p.B) * p.Hk * p.T;
+    const dim3 grid(static_cast<unsigned>((n + kDepthWarps - 1) / kDepthWarps)), block(kDepthWarps * 32);
+#define MODA_DEPTH_CASE(GG, JJ)                                                              \
+    if (p.G == GG && (p.L + 31) / 32 == JJ) {                                                 \
+        moda_bwd_depth_warp_kernel<T, HD, GG, JJ><<<grid, block, 0, stream>>>(p);            \
+        return true;                                                                          \
+    }
+    MODA_DEPTH_CASE(1, 1) MODA_DEPTH_CASE(2, 1) MODA_DEPTH_CASE(4, 1) MODA_DEPTH_CASE(8, 1)
+    MODA_DEPTH_CASE(1, 2) MODA_DEPTH_CASE(2, 2) MODA_DEPTH_CASE(4, 2) MODA_DEPTH_CASE(8, 2)
+#undef MODA_DEPTH_CASE
+    return false;
+}
+
+// The warp-per-token kernel for 16-bit inputs with d in {64, 128}, G <= 8, L <= 64
+// and 16-byte aligned unit-stride rows; false when it does not apply.
+template <typename T>
+static bool launch_depth_warp(const BwdParams& p, cudaStream_t stream) {
+    if constexpr (sizeof(T) != 2) {
+        return false;
+    } else {
+    if (p.L < 1 || p.L > 64) return false;
+    const ModaTensor* ts[7] = {&p.q, &p.dout, &p.kd, &p.vd, &p.dkd, &p.dvd, &p.dq};
+    for (const ModaTensor* x : ts) {
+        if (x->strides[3] != 1 || reinterpret_cast<uintptr_t>(x->ptr) % 16 != 0) return false;
+        for (int i = 0; i < 3; ++i)
+            if (x->sizes[i] > 1 && (x->strides[i] * 2) % 16 != 0) return false;
+    }
+    if (p.d == 128) return launch_depth_warp_hd<T, 128>(p, stream);
+    if (p.d == 64) return launch_depth_warp_hd<T, 64>(p, stream);
+    return false;
+    }
+}
+
 // Zero gradient for depth rows the forward never reads (rows >= T*L).
 template <typename T>
 __global__ void moda_bwd_zero_rows_kernel(const __grid_constant__ BwdParams p, long long r_lo) {
@@ -553,7 +740,7 @@ size_t depth_token_smem(int G, int L, int d) {
 
 template <typename T>
 static int launch_depth_t(const BwdParams& p, cudaStream_t stream) {
-    if (p.L > 0 && p.T > 0) {
+    if (p.L > 0 && p.T > 0 && !launch_depth_warp<T>(p, stream)) {
         const size_t sm = depth_token_smem(p.G, p.L, p.d);
         if (sm > 48 * 1024 &&
             cudaFuncSetAttribute(moda_bwd_depth_token_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
