@@ -19,6 +19,11 @@ region), cpu_baseline (the numpy oracle port of moda_attention_naive timed on
 this host on a bounded sample), clocks sampled during the timed region, and
 gpu_launches. ``--impl reference`` times that CPU port alone on rank 0.
 
+``--pass model`` (one GPU) times the full MoDAModel forward of the model
+configuration (d_model 2048, 16 query / 4 KV heads of 128, 24 layers, post-norm,
+FFN 4x, B=8, T=4096, bf16, random-init weights from seed 3, x ~ N(0,1)) in tokens/s,
+with the reference's cache lifecycle and again with the opt-in lean one.
+
 ``--pass backward`` (one GPU) times the backward kernels instead: one step = the
 gradients of all five inputs for a seeded dO, from the forward's O and row
 log-sum-exp (computed once, untimed). Its algorithmic FLOPs are 2.5x the
@@ -213,13 +218,16 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="kernel")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--pass", dest="which", choices=["forward", "backward"], default="forward")
+    ap.add_argument("--pass", dest="which", choices=["forward", "backward", "model"],
+                    default="forward")
     args = ap.parse_args()
     wl = WORKLOADS[args.workload]
     if args.impl == "reference":
         return run_reference(args, wl)
     if args.which == "backward":
         return run_backward(args, wl)
+    if args.which == "model":
+        return run_model(args)
     args.warmup = max(args.warmup, 3)
 
     import torch
@@ -419,10 +427,70 @@ def run_backward(args, wl):
         "roofline": {"bound": "tensor", "achieved": tflops, "peak": p_tflops, "unit": "TFLOP/s",
                      "frac": tflops / p_tflops, "peak_kind": p_kind, "traffic": None,
                      "algorithmic_flops": f_bwd,
-                     "note": "CUDA-core kernels (fp32 FMA); the tensor-core peak is the target"},
+                     "note": "tcgen05 dK/dV and dQ kernels, CUDA-core delta and depth kernels"},
         "gpu_launches": 4 * args.steps,
         "clocks": clocks.summary(),
         "verify": {"finite": finite, "device_status": device_status(dev)},
+    }
+    print(json.dumps(line), flush=True)
+
+
+MODEL_CONFIG = dict(d_model=2048, num_heads=16, num_kv_heads=4, head_dim=128, num_layers=24,
+                    chunk_size=64, max_seq_len=4096, post_norm=True)
+MODEL_B, MODEL_T, MODEL_SEED = 8, 4096, 3
+
+
+def run_model(args):
+    """Full MoDAModel forward on one GPU, reference and lean cache lifecycles."""
+    import torch
+    from moda import MoDAConfig, MoDAModel
+    from moda.kernels import device_status
+    args.warmup = max(args.warmup, 3)
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    torch.manual_seed(MODEL_SEED)
+    with torch.device(dev):
+        model = MoDAModel(MoDAConfig(**MODEL_CONFIG)).to(torch.bfloat16).eval()
+    g = torch.Generator(device=dev).manual_seed(MODEL_SEED)
+    x = torch.randn(MODEL_B, MODEL_T, MODEL_CONFIG["d_model"], device=dev, dtype=torch.bfloat16,
+                    generator=g)
+    stream = torch.cuda.current_stream(dev)
+    results, outs = {}, {}
+    for lean in (False, True):
+        model.config.lean_depth_cache = lean
+        with torch.no_grad():
+            for _ in range(args.warmup):
+                model(x)
+            torch.cuda.synchronize(dev)
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with ClockSampler(0) as clocks:
+                ev0.record(stream)
+                for _ in range(args.steps):
+                    out = model(x)
+                ev1.record(stream)
+                torch.cuda.synchronize(dev)
+        ms = ev0.elapsed_time(ev1) / args.steps
+        results[lean] = (ms, clocks.summary())
+        outs[lean] = out.float()
+    model.config.lean_depth_cache = False
+    ms, clk = results[False]
+    ms_lean, clk_lean = results[True]
+    tokens = MODEL_B * MODEL_T
+    diff = (outs[True] - outs[False]).abs()
+    line = {
+        "metric": "MoDAModel forward throughput (tokens/s)", "value": tokens / (ms * 1e-3),
+        "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic x ~ N(0,1) (seed 3), random-init weights (seed 3)",
+        "config": {"workload": "full MoDAModel forward with DepthKVCache, post-norm, FFN depth "
+                               "writes: d_model=2048 H_q=16 H_k=4 d=128 24 layers FFN 8192 "
+                               "B=8 T=4096", "global_batch": MODEL_B, "seq_len": MODEL_T},
+        "lean": {"value": tokens / (ms_lean * 1e-3), "unit": "tokens/s", "ms_per_step": ms_lean,
+                 "max_abs_diff_vs_default": float(diff.max()),
+                 "mean_abs_diff_vs_default": float(diff.mean()), "clocks": clk_lean},
+        "clocks": clk,
+        "verify": {"finite": bool(torch.isfinite(outs[False]).all()),
+                   "device_status": device_status(dev)},
     }
     print(json.dumps(line), flush=True)
 

@@ -80,6 +80,17 @@ int moda_fwd_lse(const ModaTensor* q, const ModaTensor* k, const ModaTensor* v,
                  int num_layers, float scale, int chunk_size, int dtype, int kernel,
                  moda_stream_t stream);
 
+/* Forward whose depth part is known to be all zeros: every row's softmax holds its
+ * causal keys plus zero_rows keys of score 0 whose values are 0, and nothing is read
+ * for them. Equals moda_fwd_lse with kd = vd = zeros [B,H_k,T*zero_rows,d] and
+ * num_layers = zero_rows, up to rounding. lse as in moda_fwd_lse, or NULL.
+ * The first layer of MoDAModel reads a freshly zero-filled cache (moda/model.py:
+ * 143-151, moda/cache.py:40-47, moda/attention.py:85-93); its opt-in lean cache
+ * lifecycle calls this instead of reading those zeros. No reference counterpart. */
+int moda_fwd_zero_depth(const ModaTensor* q, const ModaTensor* k, const ModaTensor* v,
+                        const ModaTensor* o, float* lse, int zero_rows, float scale, int dtype,
+                        int kernel, moda_stream_t stream);
+
 /* Bytes of device workspace moda_bwd needs (one float per query row), or -1 for
  * negative sizes. No reference counterpart. */
 int64_t moda_bwd_workspace_size(int64_t batch, int64_t num_q_heads, int64_t seq_len);

@@ -96,6 +96,7 @@ int validate_fwd(const ModaTensor* q, const ModaTensor* k, const ModaTensor* v,
     out->T = static_cast<int>(T);
     out->d = static_cast<int>(d);
     out->L = num_layers;
+    out->zero_rows = 0;
     out->scale = scale > 0.f ? scale : 1.0f / sqrtf(static_cast<float>(d));
     out->lse = nullptr;
     out->dtype = dtype;
@@ -161,6 +162,27 @@ int moda_fwd_lse(const ModaTensor* q, const ModaTensor* k, const ModaTensor* v,
     if (!lse && static_cast<int64_t>(p.B) * p.Hq * p.T > 0)
         return fail(MODA_ERR_ARG, "lse must point to B*H_q*T floats");
     p.lse = lse;
+    return launch_validated(p, kernel, static_cast<cudaStream_t>(stream));
+}
+
+int moda_fwd_zero_depth(const ModaTensor* q, const ModaTensor* k, const ModaTensor* v,
+                        const ModaTensor* o, float* lse, int zero_rows, float scale, int dtype,
+                        int kernel, moda_stream_t stream) {
+    g_err[0] = 0;
+    if (zero_rows < 0) return fail(MODA_ERR_ARG, "zero_rows must be >= 0, got %d", zero_rows);
+    if (!q || !k) return fail(MODA_ERR_ARG, "null tensor descriptor");
+    // No depth tensor: empty [B, H_k, 0, d] descriptors that nothing reads.
+    ModaTensor none;
+    memset(&none, 0, sizeof(none));
+    none.sizes[0] = q->sizes[0];
+    none.sizes[1] = k->sizes[1];
+    none.sizes[3] = q->sizes[3];
+    none.strides[3] = 1;
+    moda::FwdParams p;
+    int r = validate_fwd(q, k, v, &none, &none, o, 0, scale, dtype, &p);
+    if (r != MODA_OK) return r;
+    p.lse = lse;
+    p.zero_rows = zero_rows;
     return launch_validated(p, kernel, static_cast<cudaStream_t>(stream));
 }
 

@@ -94,6 +94,14 @@ __global__ void __launch_bounds__(kSimtRows * 32)
         consume(kdb + (r0 + li) * p.kd.strides[2], p.kd.strides[3], vdb + (r0 + li) * p.vd.strides[2],
                 p.vd.strides[3]);
 
+    if (p.zero_rows > 0) {  // zero_rows more keys of score 0 whose values are 0
+        const float m_new = fmaxf(m, 0.f);
+        const float alpha = ex2(m - m_new);
+        l = fmaf(l, alpha, static_cast<float>(p.zero_rows) * ex2(-m_new));
+#pragma unroll
+        for (int i = 0; i < kSimtMaxChunks; ++i) acc[i] *= alpha;
+        m = m_new;
+    }
     const float inv = 1.f / l;
     if (p.lse && lane == 0)  // natural log of sum_j exp(scale * q.k_j)
         p.lse[(static_cast<int64_t>(b) * p.Hq + h) * p.T + t] = (m + __log2f(l)) * kLn2;

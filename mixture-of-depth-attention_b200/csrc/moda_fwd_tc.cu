@@ -646,13 +646,19 @@ __global__ void __launch_bounds__(kThreads, 1) moda_fwd_tc_kernel(const __grid_c
             tc_fence_after();
             xsum[half * 128 + row] = l_run;
             named_bar_sync(pair_bar, 64);
-            const float l_tot = l_run + xsum[(half ^ 1) * 128 + row];
+            float l_tot = l_run + xsum[(half ^ 1) * 128 + row];
             named_bar_sync(pair_bar, 64);  // both read before the next item overwrites
-            const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
+            float m_fin = m_run, o_scale = 1.f;
+            if (p.zero_rows > 0) {  // zero_rows more keys of score 0 whose values are 0
+                m_fin = fmaxf(m_run, 0.f);
+                o_scale = exp2f(m_run - m_fin);
+                l_tot = fmaf(l_tot, o_scale, static_cast<float>(p.zero_rows) * exp2f(-m_fin));
+            }
+            const float inv = l_tot > 0.f ? o_scale / l_tot : 0.f;
             const bool valid = tok < ti.tend;
             const int head = it.hk * p.G + row % p.G;
             if (p.lse && half == 0 && valid)  // natural log of sum_j exp(scale * q.k_j)
-                p.lse[(static_cast<long long>(it.b) * p.Hq + head) * p.T + tok] = (m_run + __log2f(l_tot)) * kLn2;
+                p.lse[(static_cast<long long>(it.b) * p.Hq + head) * p.T + tok] = (m_fin + __log2f(l_tot)) * kLn2;
             uint4* dst = reinterpret_cast<uint4*>(
                 static_cast<uint16_t*>(p.o) + it.b * p.o_sb + head * p.o_sh +
                 static_cast<long long>(tok) * p.o_st + kHalfD * half);
@@ -845,6 +851,7 @@ int launch_fwd_tc(const FwdParams& p, cudaStream_t stream, char* err, size_t err
     tp.num_pairs = (p.T + 2 * n_tok - 1) / (2 * n_tok);
     tp.sc = p.scale * kLog2e;
     tp.lse = p.lse;
+    tp.zero_rows = p.zero_rows;
     const long long items = static_cast<long long>(tp.num_pairs) * p.B * p.Hk;
     if (items == 0) return MODA_OK;
     if (items > 0x7fffffffLL) {

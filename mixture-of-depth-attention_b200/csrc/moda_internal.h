@@ -11,6 +11,7 @@ struct FwdParams {
     ModaTensor q, k, v, kd, vd, o;
     float* lse;  // optional [B, H_q, T] fp32, contiguous: natural log-sum-exp per row
     int B, Hq, Hk, G, T, d, L;
+    int zero_rows;  // implicit depth rows per token with k = v = 0 (never read from memory)
     float scale;
     int dtype;
 };
@@ -44,6 +45,7 @@ struct TcParams {
     int num_items;  // num_pairs * B * Hk work items
     float sc;       // scale * log2(e)
     float* lse;     // optional [B, H_q, T] fp32 log-sum-exp output
+    int zero_rows;  // implicit all-zero depth rows per token (score 0, value 0)
 };
 
 // TMA map over a [B, H, rows, d] view (128-byte swizzle, box (64, box1, box2, 1)),

@@ -14,7 +14,7 @@ import torch.nn as nn
 from torch import Tensor
 
 from .config import MoDAConfig
-from .kernels.moda_cuda import moda_attention_cuda
+from .kernels.moda_cuda import moda_attention_cuda, moda_attention_zero_depth
 
 
 class MoDAAttention(nn.Module):
@@ -44,16 +44,24 @@ class MoDAAttention(nn.Module):
         self.dropout = nn.Dropout(config.dropout) if config.dropout > 0 else nn.Identity()
 
     def forward(self, x: Tensor, K_depth: Optional[Tensor] = None,
-                V_depth: Optional[Tensor] = None) -> tuple[Tensor, Tensor, Tensor]:
+                V_depth: Optional[Tensor] = None, *, zero_depth_rows: int = 0,
+                write_tokens: Optional[int] = None) -> tuple[Tensor, Tensor, Tensor]:
         """Forward pass.
 
         Args:
             x: [B, T, D] input (CUDA).
             K_depth: [B, H_k, T*L', d] depth keys from preceding layers, or None.
             V_depth: [B, H_k, T*L', d] depth values, or None.
+            zero_depth_rows: keyword-only, not in the reference. With no depth
+                tensors, attend to this many all-zero depth rows per token (what a
+                zero-filled cache holds) without reading them.
+            write_tokens: keyword-only, not in the reference. Return k_write/v_write
+                for the first ``write_tokens`` tokens only (None: all T; 0: skip the
+                two depth projections).
 
         Returns:
-            (output [B, T, D], k_write [B, H_k, T, d], v_write [B, H_k, T, d]).
+            (output [B, T, D], k_write [B, H_k, T', d], v_write [B, H_k, T', d]),
+            T' = T unless ``write_tokens`` is given.
         """
         B, T, D = x.shape
         H_q, H_k, d = self.num_heads, self.num_kv_heads, self.head_dim
@@ -61,17 +69,35 @@ class MoDAAttention(nn.Module):
         Q = self.q_proj(x).view(B, T, H_q, d).transpose(1, 2)
         K = self.k_proj(x).view(B, T, H_k, d).transpose(1, 2)
         V = self.v_proj(x).view(B, T, H_k, d).transpose(1, 2)
-        k_write = self.k_depth_proj(x).view(B, T, H_k, d).transpose(1, 2)
-        v_write = self.v_depth_proj(x).view(B, T, H_k, d).transpose(1, 2)
+        n_w = T if write_tokens is None else max(0, min(int(write_tokens), T))
+        if n_w > 0:
+            # projected over all T tokens: a token slice of a batched x is strided and
+            # would cost a copy larger than the GEMM work it saves
+            k_write = self.k_depth_proj(x).view(B, T, H_k, d).transpose(1, 2)[:, :, :n_w]
+            v_write = self.v_depth_proj(x).view(B, T, H_k, d).transpose(1, 2)[:, :, :n_w]
+        else:
+            k_write = v_write = x.new_empty(B, H_k, 0, d)
 
+        # Without autograd the kernel writes O straight into the [B, T, H_q, d] layout
+        # o_proj reads (its output strides are free), which replaces the reference's
+        # transpose + contiguous copy (attention.py:98) with nothing.
+        o_bt = None if torch.is_grad_enabled() else Q.new_empty(B, T, H_q, d)
+        dst = None if o_bt is None else o_bt.transpose(1, 2)
         if K_depth is not None and V_depth is not None and K_depth.shape[2] > 0:
             out = moda_attention_cuda(Q, K, V, K_depth, V_depth, num_layers=self.num_layers,
-                                      scale=self.scale, chunk_size=self.config.chunk_size)
+                                      scale=self.scale, chunk_size=self.config.chunk_size,
+                                      out=dst)
+        elif zero_depth_rows > 0:
+            out = moda_attention_zero_depth(Q, K, V, zero_depth_rows, scale=self.scale, out=dst)
         else:
             empty = Q.new_empty(B, H_k, 0, d)
-            out = moda_attention_cuda(Q, K, V, empty, empty, num_layers=0, scale=self.scale)
+            out = moda_attention_cuda(Q, K, V, empty, empty, num_layers=0, scale=self.scale,
+                                      out=dst)
 
-        out = out.transpose(1, 2).contiguous().view(B, T, H_q * d)
+        if o_bt is not None:
+            out = o_bt.view(B, T, H_q * d)
+        else:
+            out = out.transpose(1, 2).contiguous().view(B, T, H_q * d)
         out = self.o_proj(out)
         out = self.dropout(out)
         return out, k_write, v_write

@@ -20,23 +20,43 @@ class DepthKVCache:
     Same constructor, ``write``, ``read`` and ``reset`` as the reference. The
     buffers are zero-initialised like the reference's (cache.py:38-47), so
     unwritten slots read as zeros.
+
+    ``zero_prefix_rows`` (keyword-only, not in the reference): zero only rows
+    [0, zero_prefix_rows) of each (batch, head) and leave the rest uninitialised,
+    for a caller that never reads unwritten rows past that prefix.
     """
 
     def __init__(self, batch_size: int, max_seq_len: int, num_layers: int, num_kv_heads: int,
                  head_dim: int, device: Optional[torch.device] = None,
-                 dtype: Optional[torch.dtype] = None):
+                 dtype: Optional[torch.dtype] = None, *,
+                 zero_prefix_rows: Optional[int] = None):
         self.batch_size = batch_size
         self.max_seq_len = max_seq_len
         self.num_layers = num_layers
         self.num_kv_heads = num_kv_heads
         self.head_dim = head_dim
         total_depth = max_seq_len * num_layers
-        self.k_cache = torch.zeros(batch_size, num_kv_heads, total_depth, head_dim,
-                                   device=device, dtype=dtype)
-        self.v_cache = torch.zeros(batch_size, num_kv_heads, total_depth, head_dim,
-                                   device=device, dtype=dtype)
+        shape = (batch_size, num_kv_heads, total_depth, head_dim)
+        if zero_prefix_rows is None:
+            self.k_cache = torch.zeros(shape, device=device, dtype=dtype)
+            self.v_cache = torch.zeros(shape, device=device, dtype=dtype)
+        else:
+            self.k_cache = torch.empty(shape, device=device, dtype=dtype)
+            self.v_cache = torch.empty(shape, device=device, dtype=dtype)
+            n = max(0, min(int(zero_prefix_rows), total_depth))
+            for buf in (self.k_cache, self.v_cache):
+                if n == 0:
+                    continue
+                if batch_size * num_kv_heads <= 64:
+                    # one contiguous run per (batch, head): the fill's fast path
+                    for b in range(batch_size):
+                        for h in range(num_kv_heads):
+                            buf[b, h, :n].zero_()
+                else:
+                    buf[:, :, :n].zero_()
         self._layer_count = 0
         self._seq_len = 0
+        self._written = False  # any write since construction / reset
 
     def write(self, layer_idx: int, k_depth: Tensor, v_depth: Tensor,
               seq_len: Optional[int] = None):
@@ -50,6 +70,7 @@ class DepthKVCache:
         """
         T = seq_len or k_depth.shape[2]
         self._seq_len = max(self._seq_len, T)
+        self._written = True
         depth_append(self.k_cache, self.v_cache, layer_idx, k_depth, v_depth,
                      self.num_layers, T)
 
@@ -65,3 +86,4 @@ class DepthKVCache:
         self.v_cache.zero_()
         self._layer_count = 0
         self._seq_len = 0
+        self._written = False

@@ -24,6 +24,13 @@ class MoDAConfig:
         use_triton: Accepted for API parity and ignored: CUDA tensors always run
             the B200 kernel.
         post_norm: Use post-norm (True) vs pre-norm (False).
+        lean_depth_cache: Opt-in (not in the reference; default False keeps its
+            behaviour). MoDAModel then skips the depth-cache work whose result no
+            layer reads: the zero-fill of cache rows the attention never addresses,
+            writes into those rows and their projections, the last layer's writes,
+            and the first layer's read of an all-zero cache (computed as implicit
+            zero rows instead). Outputs equal the default up to floating-point
+            rounding of the first layer's softmax sum.
     """
 
     d_model: int = 768
@@ -37,6 +44,7 @@ class MoDAConfig:
     max_seq_len: int = 2048
     use_triton: bool = False
     post_norm: bool = True
+    lean_depth_cache: bool = False
 
     def __post_init__(self):
         if self.num_kv_heads is None:

@@ -21,7 +21,8 @@ MODA_ERR_ARG, MODA_ERR_SHAPE, MODA_ERR_DEPTH_ROWS = -1, -2, -3
 MODA_ERR_DTYPE, MODA_ERR_LAUNCH, MODA_ERR_UNSUPPORTED = -4, -5, -6
 KERNEL_AUTO, KERNEL_TC, KERNEL_SIMT = 0, 1, 2
 
-EXPORTED_SYMBOLS = ("moda_fwd", "moda_fwd_ex", "moda_fwd_lse", "moda_fwd_plan", "moda_bwd",
+EXPORTED_SYMBOLS = ("moda_fwd", "moda_fwd_ex", "moda_fwd_lse", "moda_fwd_zero_depth",
+                    "moda_fwd_plan", "moda_bwd",
                     "moda_bwd_noalloc", "moda_bwd_workspace_size", "moda_depth_append",
                     "moda_last_error", "moda_device_status", "moda_version")
 NOALLOC_ROWS = 1 << 20   # MODA_NOALLOC_ROWS
@@ -63,6 +64,8 @@ def load():
         lib.moda_fwd_ex.restype = i
         lib.moda_fwd_lse.argtypes = [T, T, T, T, T, T, vp, i, f, i, i, i, vp]
         lib.moda_fwd_lse.restype = i
+        lib.moda_fwd_zero_depth.argtypes = [T, T, T, T, vp, i, f, i, i, vp]
+        lib.moda_fwd_zero_depth.restype = i
         i64 = ctypes.c_int64
         lib.moda_bwd_workspace_size.argtypes = [i64, i64, i64]
         lib.moda_bwd_workspace_size.restype = i64

@@ -50,6 +50,13 @@ def _check_inputs(Q, K, V, K_depth, V_depth):
             raise TypeError(f"{n} has dtype {t.dtype}, Q has {dt}")
 
 
+def _check_out(out: Tensor, Q: Tensor) -> Tensor:
+    if not isinstance(out, Tensor) or out.shape != Q.shape or out.dtype != Q.dtype or \
+            out.device != Q.device:
+        raise _lib.MoDAShapeError("out must be a tensor with Q's shape, dtype and device")
+    return out
+
+
 def moda_forward_into(O: Tensor, Q: Tensor, K: Tensor, V: Tensor, K_depth: Tensor,
                       V_depth: Tensor, num_layers: int, scale: Optional[float] = None,
                       chunk_size: Optional[int] = None, kernel: str = "auto") -> Tensor:
@@ -154,7 +161,8 @@ class _MoDAFunction(torch.autograd.Function):
 
 def moda_attention_cuda(Q: Tensor, K: Tensor, V: Tensor, K_depth: Tensor, V_depth: Tensor,
                         num_layers: int, scale: Optional[float] = None,
-                        chunk_size: Optional[int] = None, *, kernel: str = "auto") -> Tensor:
+                        chunk_size: Optional[int] = None, *, kernel: str = "auto",
+                        out: Optional[Tensor] = None) -> Tensor:
     """MoDA attention: fused sequence + depth attention with one combined softmax.
 
     Args:
@@ -165,9 +173,13 @@ def moda_attention_cuda(Q: Tensor, K: Tensor, V: Tensor, K_depth: Tensor, V_dept
         scale: softmax scale, default d**-0.5 (moda_naive.py:48-49).
         chunk_size: accepted for signature parity; the result does not depend on it.
         kernel: "auto" (default), "tc" or "simt" to force a kernel.
+        out: keyword-only, not in the reference. Destination [B, H_q, T, d] of Q's
+            dtype and device, any strides (e.g. the transposed view of a
+            [B, T, H_q, d] buffer, the layout the output projection reads). Only
+            without autograd.
 
     Returns:
-        [B, H_q, T, d] contiguous tensor of Q's dtype.
+        [B, H_q, T, d] tensor of Q's dtype: ``out``, or a new contiguous tensor.
     """
     if kernel not in _KERNELS:
         raise ValueError(f"kernel must be one of {sorted(_KERNELS)}")
@@ -177,11 +189,76 @@ def moda_attention_cuda(Q: Tensor, K: Tensor, V: Tensor, K_depth: Tensor, V_dept
     needs_grad = torch.is_grad_enabled() and any(
         t.requires_grad for t in (Q, K, V, K_depth, V_depth))
     if needs_grad:
+        if out is not None:
+            raise ValueError("out= is only supported when no gradient is needed")
         return _MoDAFunction.apply(Q, K, V, K_depth, V_depth, int(num_layers), scale,
                                    chunk_size, kernel)
-    O = torch.empty(Q.shape, dtype=Q.dtype, device=Q.device)
+    O = torch.empty(Q.shape, dtype=Q.dtype, device=Q.device) if out is None else _check_out(out, Q)
     return moda_forward_into(O, Q, K, V, K_depth, V_depth, int(num_layers), scale, chunk_size,
                              kernel)
+
+
+def moda_forward_zero_depth(Q: Tensor, K: Tensor, V: Tensor, zero_rows: int,
+                            scale: Optional[float] = None, kernel: str = "auto",
+                            out: Optional[Tensor] = None):
+    """Forward whose depth part is ``zero_rows`` all-zero rows per token, none read.
+
+    Equals ``moda_forward_lse`` with K_depth = V_depth = zeros [B,H_k,T*zero_rows,d]
+    and num_layers = zero_rows, up to rounding. Returns (O, lse); O is ``out`` (any
+    strides) when given.
+    """
+    empty = Q.new_empty(Q.shape[0], K.shape[1], 0, Q.shape[3])
+    _check_inputs(Q, K, V, empty, empty)
+    if int(zero_rows) < 0:
+        raise ValueError(f"zero_rows must be >= 0, got {zero_rows}")
+    O = torch.empty(Q.shape, dtype=Q.dtype, device=Q.device) if out is None else _check_out(out, Q)
+    lse = torch.empty(Q.shape[:3], dtype=torch.float32, device=Q.device)
+    lib = _lib.load()
+    stream = torch.cuda.current_stream(Q.device).cuda_stream
+    with torch.cuda.device(Q.device):
+        code = lib.moda_fwd_zero_depth(_desc(Q), _desc(K), _desc(V), _desc(O), lse.data_ptr(),
+                                       int(zero_rows), float(scale) if scale else 0.0,
+                                       _DTYPES[Q.dtype], _KERNELS[kernel], stream)
+    _lib.check(code, "moda_fwd_zero_depth")
+    return O, lse
+
+
+class _ZeroDepthFunction(torch.autograd.Function):
+    """Autograd for the implicit-zero depth forward. The zero rows have no tensor and
+    contribute nothing to dQ (their keys are 0), so the backward is the L = 0 backward
+    with this forward's log-sum-exp, which already counts them."""
+
+    @staticmethod
+    def forward(ctx, Q, K, V, zero_rows, scale, kernel):
+        O, lse = moda_forward_zero_depth(Q, K, V, zero_rows, scale, kernel)
+        ctx.save_for_backward(Q, K, V, O, lse)
+        ctx.scale = scale
+        return O
+
+    @staticmethod
+    def backward(ctx, dO):
+        Q, K, V, O, lse = ctx.saved_tensors
+        empty = Q.new_empty(Q.shape[0], K.shape[1], 0, Q.shape[3])
+        dQ, dK, dV, _, _ = moda_backward(dO, Q, K, V, empty, empty, O, lse, 0, ctx.scale)
+        return dQ, dK, dV, None, None, None
+
+
+def moda_attention_zero_depth(Q: Tensor, K: Tensor, V: Tensor, zero_rows: int,
+                              scale: Optional[float] = None, *, kernel: str = "auto",
+                              out: Optional[Tensor] = None) -> Tensor:
+    """``moda_attention_cuda`` over an all-zero depth part of ``zero_rows`` rows per
+    token, without the depth tensors: each row's softmax also holds ``zero_rows`` keys
+    of score 0 with value 0. What the first layer of ``MoDAModel`` computes from its
+    freshly zero-filled cache (moda/model.py:143-151, moda/cache.py:40-47).
+    ``out`` as in ``moda_attention_cuda``."""
+    if kernel not in _KERNELS:
+        raise ValueError(f"kernel must be one of {sorted(_KERNELS)}")
+    needs_grad = torch.is_grad_enabled() and any(t.requires_grad for t in (Q, K, V))
+    if needs_grad:
+        if out is not None:
+            raise ValueError("out= is only supported when no gradient is needed")
+        return _ZeroDepthFunction.apply(Q, K, V, int(zero_rows), scale, kernel)
+    return moda_forward_zero_depth(Q, K, V, zero_rows, scale, kernel, out)[0]
 
 
 def depth_append(k_cache: Tensor, v_cache: Tensor, layer_idx: int, k: Tensor, v: Tensor,

@@ -157,3 +157,18 @@ def test_bwd_rejects_bad_arguments_before_launch(case):
         expect = _lib.MODA_ERR_ARG
     assert lib.moda_bwd(*args) == expect
     assert lib.moda_last_error() != b""
+
+
+@pytest.mark.parametrize("case", ["negative_rows", "k_heads", "o_shape"])
+def test_zero_depth_rejects_bad_arguments_before_launch(case):
+    lib = _lib.load()
+    B, Hq, Hk, T, d = 1, 4, 2, 8, 64
+    Q, O = _t((B, Hq, T, d)), _t((B, Hq, T, d) if case != "o_shape" else (B, Hq, T + 1, d))
+    K, V = _t((B, Hk, T, d)), _t((B, Hk if case != "k_heads" else 3, T, d))
+    D = lambda x: _lib.describe(x.data_ptr(), x.shape, x.stride())
+    lse = torch.empty(B, Hq, T)
+    rows = -1 if case == "negative_rows" else 4
+    code = lib.moda_fwd_zero_depth(D(Q), D(K), D(V), D(O), lse.data_ptr(), rows, 0.0,
+                                   _lib.MODA_BF16, _lib.KERNEL_AUTO, None)
+    assert code == (_lib.MODA_ERR_ARG if case == "negative_rows" else _lib.MODA_ERR_SHAPE)
+    assert lib.moda_last_error() != b""

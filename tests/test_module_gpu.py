@@ -191,3 +191,31 @@ def test_model_bf16_runs_the_tensor_core_kernel():
     with torch.no_grad():
         out = model(torch.randn(2, 200, 512, device="cuda", dtype=torch.bfloat16))
     assert torch.isfinite(out).all()
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_output_written_in_projection_layout_equals_contiguous(dtype):
+    # without autograd MoDAAttention has the kernel write O as [B, T, H_q, d] (the
+    # layout o_proj reads) instead of copying a [B, H_q, T, d] result
+    from moda.kernels import moda_attention_cuda
+    torch.manual_seed(0)
+    B, Hq, Hk, T, d, L = 2, 8, 2, 160, 128, 3
+    Q = torch.randn(B, T, Hq, d, device="cuda", dtype=dtype).transpose(1, 2)
+    K = torch.randn(B, Hk, T, d, device="cuda", dtype=dtype)
+    V = torch.randn(B, Hk, T, d, device="cuda", dtype=dtype)
+    Kd = torch.randn(B, Hk, T * L, d, device="cuda", dtype=dtype)
+    Vd = torch.randn(B, Hk, T * L, d, device="cuda", dtype=dtype)
+    ref = moda_attention_cuda(Q, K, V, Kd, Vd, L)
+    o_bt = torch.empty(B, T, Hq, d, device="cuda", dtype=dtype)
+    got = moda_attention_cuda(Q, K, V, Kd, Vd, L, out=o_bt.transpose(1, 2))
+    assert got.data_ptr() == o_bt.data_ptr()
+    assert torch.equal(o_bt.transpose(1, 2), ref)
+
+    cfg = MoDAConfig(d_model=256, num_heads=4, num_kv_heads=2, head_dim=64, num_layers=3)
+    attn = MoDAAttention(cfg).cuda().to(dtype)
+    x = torch.randn(B, 64, 256, device="cuda", dtype=dtype)
+    kd = torch.randn(B, 2, 64 * 3, 64, device="cuda", dtype=dtype)
+    with torch.no_grad():
+        fast = attn(x, kd, kd)[0]
+    slow = attn(x, kd, kd)[0].detach()  # grad enabled: the copying path
+    assert torch.equal(fast, slow)
