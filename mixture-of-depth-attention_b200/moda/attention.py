@@ -83,6 +83,14 @@ class MoDAAttention(nn.Module):
         # transpose + contiguous copy (attention.py:98) with nothing.
         o_bt = None if torch.is_grad_enabled() else Q.new_empty(B, T, H_q, d)
         dst = None if o_bt is None else o_bt.transpose(1, 2)
+        if K_depth is not None and V_depth is not None and K_depth.shape[2] > 0 and \
+                torch.is_grad_enabled():
+            # The depth views alias the cache, which later layers write in place; the
+            # backward must see the rows as they are now (the reference's autograd
+            # keeps its own copies), so the addressed rows are snapshot here.
+            rows = T * self.num_layers
+            K_depth = K_depth[:, :, :rows].clone()
+            V_depth = V_depth[:, :, :rows].clone()
         if K_depth is not None and V_depth is not None and K_depth.shape[2] > 0:
             out = moda_attention_cuda(Q, K, V, K_depth, V_depth, num_layers=self.num_layers,
                                       scale=self.scale, chunk_size=self.config.chunk_size,

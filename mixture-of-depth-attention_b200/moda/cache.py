@@ -11,7 +11,7 @@ from typing import Optional
 import torch
 from torch import Tensor
 
-from .kernels.moda_cuda import depth_append
+from .kernels.moda_cuda import depth_append, depth_append_autograd
 
 
 class DepthKVCache:
@@ -71,8 +71,16 @@ class DepthKVCache:
         T = seq_len or k_depth.shape[2]
         self._seq_len = max(self._seq_len, T)
         self._written = True
-        depth_append(self.k_cache, self.v_cache, layer_idx, k_depth, v_depth,
-                     self.num_layers, T)
+        if torch.is_grad_enabled() and (k_depth.requires_grad or v_depth.requires_grad or
+                                        self.k_cache.requires_grad or
+                                        self.v_cache.requires_grad):
+            # training: the write is part of the graph, as the reference's slice
+            # assignment is (gradients reach k_depth / v_depth and their projections)
+            self.k_cache, self.v_cache = depth_append_autograd(
+                self.k_cache, self.v_cache, layer_idx, k_depth, v_depth, self.num_layers, T)
+        else:
+            depth_append(self.k_cache, self.v_cache, layer_idx, k_depth, v_depth,
+                         self.num_layers, T)
 
     def read(self, seq_len: Optional[int] = None) -> tuple[Tensor, Tensor]:
         """Views [B, H_k, T*L, d] of the first T tokens' depth rows (cache.py:76-88)."""

@@ -284,6 +284,44 @@ def depth_append(k_cache: Tensor, v_cache: Tensor, layer_idx: int, k: Tensor, v:
     _lib.check(code, "moda_depth_append")
 
 
+class _DepthAppendFunction(torch.autograd.Function):
+    """In-place depth append that autograd sees, like the reference's strided slice
+    assignment into the cache (moda/cache.py:73-74, recorded by torch as a copy into
+    slices): the rows written get their gradient from the cache's gradient, and the
+    cache's earlier content gets the rest. The forward is the CUDA append kernel."""
+
+    @staticmethod
+    def forward(ctx, k_cache, v_cache, k, v, layer_idx, num_layers, seq_len):
+        depth_append(k_cache, v_cache, layer_idx, k, v, num_layers, seq_len)
+        ctx.mark_dirty(k_cache, v_cache)
+        ctx.meta = (layer_idx, num_layers, seq_len, k.shape, v.shape)
+        return k_cache, v_cache
+
+    @staticmethod
+    def backward(ctx, g_kc, g_vc):
+        slot, L, T, k_shape, v_shape = ctx.meta
+
+        def split(g, src_shape):
+            if g is None:
+                return None, None
+            g_src = g.new_zeros(src_shape)
+            g_src[:, :, :T] = g[:, :, slot:T * L:L]
+            g_prev = g.clone()
+            g_prev[:, :, slot:T * L:L] = 0  # overwritten rows: nothing flows further back
+            return g_prev, g_src
+
+        gk_prev, gk = split(g_kc, k_shape)
+        gv_prev, gv = split(g_vc, v_shape)
+        return gk_prev, gv_prev, gk, gv, None, None, None
+
+
+def depth_append_autograd(k_cache: Tensor, v_cache: Tensor, layer_idx: int, k: Tensor,
+                          v: Tensor, num_layers: int, seq_len: int):
+    """``depth_append`` recorded by autograd; returns the (same, now dirty) caches."""
+    return _DepthAppendFunction.apply(k_cache, v_cache, k, v, int(layer_idx), int(num_layers),
+                                      int(seq_len))
+
+
 def device_status(device=None) -> int:
     """Read and clear the kernels' timeout status word (0 = no bounded wait expired)."""
     stream = torch.cuda.current_stream(device).cuda_stream

@@ -109,6 +109,33 @@ def model_case(post_norm):
     return f"model_{'post' if post_norm else 'pre'}norm", arrays, meta
 
 
+def model_grad_case(post_norm):
+    """Parameter and input gradients of a 3-layer reference MoDAModel (fp64 autograd).
+
+    With 3 layers, later layers write cache rows that earlier layers read (the 2N-slot
+    cache addressed with L = N), so the gradients cover the autograd path through the
+    in-place cache writes (moda/cache.py:73-74) as well as the attention."""
+    from moda.config import MoDAConfig
+    from moda.model import MoDAModel
+    torch.manual_seed(5)
+    conf = dict(d_model=32, num_heads=4, num_kv_heads=2, num_layers=3, max_seq_len=16,
+                post_norm=post_norm)
+    model = MoDAModel(MoDAConfig(**conf)).double()
+    g = torch.Generator().manual_seed(19)
+    # fp32-representable inputs, so the fp32 fixture holds them exactly
+    x = torch.randn(2, 9, 32, generator=g).double().requires_grad_()
+    w = torch.randn(2, 9, 32, generator=g).double()
+    out = model(x)
+    (out * w).sum().backward()
+    f32 = lambda t: t.detach().float().numpy()  # weights start as fp32; fp32 keeps 1e-7
+    arrays = {f"w.{k}": f32(v) for k, v in model.state_dict().items()}
+    arrays |= {f"g.{k}": f32(p.grad) for k, p in model.named_parameters() if p.grad is not None}
+    arrays |= dict(x=f32(x), loss_weight=f32(w), out=f32(out), x_grad=f32(x.grad))
+    meta = dict(kind="model_grad", config=conf,
+                no_grad_params=[k for k, p in model.named_parameters() if p.grad is None])
+    return f"model_grad_{'post' if post_norm else 'pre'}norm", arrays, meta
+
+
 def cache_case():
     from moda.cache import DepthKVCache
     B, T, L, H_k, d = 2, 5, 3, 2, 8
@@ -163,12 +190,14 @@ def main():
         module_case(),
         model_case(True),
         model_case(False),
+        model_grad_case(True),
+        model_grad_case(False),
         cache_case(),
     ]
     for name, arrays, meta in cases:
         meta["torch"] = torch.__version__
         meta["source"] = ("reference moda (sahilmalik27/mixture-of-depth-attention), CPU "
-                          + ("fp64 autograd" if meta["kind"] == "grad" else "fp32"))
+                          + ("fp64 autograd" if meta["kind"] in ("grad", "model_grad") else "fp32"))
         path = os.path.join(HERE, name + ".npz")
         np.savez_compressed(path, meta=np.array(json.dumps(meta)), **arrays)
         print(f"{name}: {os.path.getsize(path)} bytes, keys={sorted(arrays)[:8]}...")

@@ -143,3 +143,28 @@ def test_module_gradient_through_depth():
     for t in (x, Kd, Vd):
         assert t.grad is not None and torch.isfinite(t.grad).all()
         assert float(t.grad.abs().max()) > 0
+
+
+@pytest.mark.parametrize("lean", [False, True])
+@pytest.mark.parametrize("name", ["model_grad_postnorm", "model_grad_prenorm"])
+def test_model_gradients_match_reference(name, lean):
+    # 3-layer MoDAModel trained through the depth cache: gradients reach every depth
+    # projection whose rows a later layer reads (through the in-place cache writes), and
+    # every attention sees the cache as it was when it read it. Reference: fp64 autograd.
+    from helpers import load_golden
+    from moda import MoDAConfig, MoDAModel
+    z, meta = load_golden(name)
+    model = MoDAModel(MoDAConfig(**meta["config"], lean_depth_cache=lean))
+    model.load_state_dict({k[2:]: torch.from_numpy(z[k]) for k in z.files if k.startswith("w.")})
+    model = model.cuda()
+    x = torch.from_numpy(z["x"]).cuda().requires_grad_()
+    out = model(x)
+    (out * torch.from_numpy(z["loss_weight"]).cuda()).sum().backward()
+    assert rel_err(out.detach().cpu().numpy(), z["out"]) <= FP32_REL_TOL
+    assert rel_err(x.grad.cpu().numpy(), z["x_grad"]) <= FP32_REL_TOL
+    for pname, p in model.named_parameters():
+        if pname in meta["no_grad_params"]:
+            assert p.grad is None or not p.grad.any(), pname
+        else:
+            assert p.grad is not None, pname
+            assert rel_err(p.grad.cpu().numpy(), z["g." + pname]) <= FP32_REL_TOL, pname
