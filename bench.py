@@ -24,6 +24,11 @@ configuration (d_model 2048, 16 query / 4 KV heads of 128, 24 layers, post-norm,
 FFN 4x, B=8, T=4096, bf16, random-init weights from seed 3, x ~ N(0,1)) in tokens/s,
 with the reference's cache lifecycle and again with the opt-in lean one.
 
+``--pass proj`` (one GPU) times the fused depth-write projection of one model layer
+(x [B=8, T=4096, 2048] times the stacked k/v depth weights [1024, 2048], written into
+cache slot 5 of a [8, 4, 4096*48, 128] cache) against the same work as two library
+GEMMs plus the append kernel; ``--batch`` shrinks B for profiling.
+
 ``--pass backward`` (one GPU) times the backward kernels instead: one step = the
 gradients of all five inputs for a seeded dO, from the forward's O and row
 log-sum-exp (computed once, untimed). Its algorithmic FLOPs are 2.5x the
@@ -218,8 +223,11 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="kernel")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--pass", dest="which", choices=["forward", "backward", "model"],
+    ap.add_argument("--pass", dest="which", choices=["forward", "backward", "model", "proj"],
                     default="forward")
+    ap.add_argument("--batch", type=int, default=None, help="batch override for --pass proj")
+    ap.add_argument("--kernel-shares", action="store_true",
+                    help="--pass model: also print each path's per-kernel CUDA time (stderr)")
     args = ap.parse_args()
     wl = WORKLOADS[args.workload]
     if args.impl == "reference":
@@ -228,6 +236,8 @@ def main():
         return run_backward(args, wl)
     if args.which == "model":
         return run_model(args)
+    if args.which == "proj":
+        return run_proj(args)
     args.warmup = max(args.warmup, 3)
 
     import torch
@@ -472,6 +482,17 @@ def run_model(args):
         ms = ev0.elapsed_time(ev1) / args.steps
         results[lean] = (ms, clocks.summary())
         outs[lean] = out.float()
+    if args.kernel_shares:  # one untimed forward per path under the CUDA activity profiler
+        from torch.profiler import ProfilerActivity, profile
+        for lean in (False, True):
+            model.config.lean_depth_cache = lean
+            with torch.no_grad(), profile(activities=[ProfilerActivity.CUDA]) as prof:
+                model(x)
+                torch.cuda.synchronize(dev)
+            print(f"--- kernel shares, {'lean' if lean else 'default'} cache lifecycle",
+                  file=sys.stderr)
+            print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=12,
+                                            max_name_column_width=60), file=sys.stderr)
     model.config.lean_depth_cache = False
     ms, clk = results[False]
     ms_lean, clk_lean = results[True]
@@ -491,6 +512,73 @@ def run_model(args):
         "clocks": clk,
         "verify": {"finite": bool(torch.isfinite(outs[False]).all()),
                    "device_status": device_status(dev)},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_proj(args):
+    """Fused depth-write projection (one model layer's shape) on one GPU."""
+    import torch
+    import torch.nn.functional as F
+    from moda.kernels import device_status
+    from moda.kernels.moda_cuda import depth_append, depth_proj_append
+    args.warmup = max(args.warmup, 3)
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B = args.batch or MODEL_B
+    T, D = MODEL_T, MODEL_CONFIG["d_model"]
+    Hk, d, Lc, slot = MODEL_CONFIG["num_kv_heads"], MODEL_CONFIG["head_dim"], 48, 5
+    g = torch.Generator(device=dev).manual_seed(MODEL_SEED)
+    x = torch.randn(B, T, D, device=dev, generator=g).to(torch.bfloat16)
+    w = (torch.randn(2 * Hk * d, D, device=dev, generator=g) / D ** 0.5).to(torch.bfloat16)
+    kc = torch.zeros(B, Hk, T * Lc, d, device=dev, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    stream = torch.cuda.current_stream(dev)
+
+    def fused():
+        depth_proj_append(x, w, kc, vc, slot, Lc, T)
+
+    def unfused():
+        k = F.linear(x, w[:Hk * d]).view(B, T, Hk, d).transpose(1, 2)
+        v = F.linear(x, w[Hk * d:]).view(B, T, Hk, d).transpose(1, 2)
+        depth_append(kc, vc, slot, k, v, Lc, T)
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(0) as clocks:
+            e0.record(stream)
+            for _ in range(args.steps):
+                fn()
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / args.steps, clocks.summary()
+
+    ms, clk = timed(fused)
+    ms_ref, _ = timed(unfused)
+    k_fused = kc[:, :, slot:T * Lc:Lc].clone()
+    unfused()
+    torch.cuda.synchronize(dev)
+    same = bool(torch.equal(k_fused, kc[:, :, slot:T * Lc:Lc]))
+    flop = 2.0 * B * T * D * 2 * Hk * d
+    tflops = flop / (ms * 1e-3) / 1e12
+    p_tflops, _, p_kind = peaks()
+    line = {
+        "metric": "fused depth-write projection + cache append (TFLOP/s)", "value": tflops,
+        "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic N(0,1) x, N(0, 1/D) weights (seed 3)",
+        "config": {"workload": f"depth-write projection of one model layer: x [{B},{T},{D}] "
+                               f"x W[{2 * Hk * d},{D}]^T into cache rows t*{Lc}+{slot}"},
+        "roofline": {"bound": "tensor", "achieved": tflops, "peak": p_tflops, "unit": "TFLOP/s",
+                     "frac": tflops / p_tflops, "peak_kind": p_kind},
+        "unfused": {"ms_per_step": ms_ref, "value": flop / (ms_ref * 1e-3) / 1e12,
+                    "what": "two library GEMMs (torch F.linear) + moda_depth_append"},
+        "gpu_launches": args.steps,
+        "clocks": clk,
+        "verify": {"bit_equal_to_unfused": same, "device_status": device_status(dev)},
     }
     print(json.dumps(line), flush=True)
 

@@ -149,6 +149,23 @@ int moda_depth_append(const ModaTensor* k_src, const ModaTensor* v_src, const Mo
                       const ModaTensor* v_cache, int layer_idx, int num_layers, int seq_len,
                       int dtype, moda_stream_t stream);
 
+/*
+ * Depth-write projection with the depth-cache append in its epilogue:
+ *   y = x . w^T, x [B,1,T,D], w [1,1,2*H_k*d,D] (the H_k*d k rows, then the v rows);
+ *   k_cache[b,h,t*L + layer_idx,:] = y[b,t,h*d : (h+1)*d]
+ *   v_cache[b,h,t*L + layer_idx,:] = y[b,t,(H_k+h)*d : (H_k+h+1)*d]   for t < seq_len.
+ * H_k and d come from the caches [B,H_k,>=seq_len*L,d]; no other cache row is touched.
+ * bf16/f16 with fp32 accumulation (tcgen05); needs d a multiple of 32, D a multiple of
+ * 8, unit stride along the last dimension and 16-byte aligned strides, else
+ * MODA_ERR_UNSUPPORTED before any launch.
+ * Replaces k_depth_proj / v_depth_proj (moda/attention.py:81-82) or ffn_k_depth_proj /
+ * ffn_v_depth_proj (moda/model.py:78-81, 92-95) followed by DepthKVCache.write
+ * (moda/cache.py:52-74).
+ */
+int moda_depth_proj_append(const ModaTensor* x, const ModaTensor* w, const ModaTensor* k_cache,
+                           const ModaTensor* v_cache, int layer_idx, int num_layers, int seq_len,
+                           int dtype, moda_stream_t stream);
+
 /* Text of the last error on the calling thread ("" if none). Thread-local. */
 const char* moda_last_error(void);
 

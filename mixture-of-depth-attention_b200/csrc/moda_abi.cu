@@ -347,11 +347,81 @@ int moda_depth_append(const ModaTensor* k_src, const ModaTensor* v_src, const Mo
 const char* moda_last_error(void) { return g_err; }
 
 int moda_device_status(moda_stream_t stream) {
-    int v = 0, w = 0;
-    if (moda::read_and_clear_status(static_cast<cudaStream_t>(stream), &v) != cudaSuccess ||
-        moda::read_and_clear_bwd_status(static_cast<cudaStream_t>(stream), &w) != cudaSuccess)
+    int v = 0, w = 0, x = 0;
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (moda::read_and_clear_status(st, &v) != cudaSuccess ||
+        moda::read_and_clear_bwd_status(st, &w) != cudaSuccess ||
+        moda::read_and_clear_proj_status(st, &x) != cudaSuccess)
         return fail(MODA_ERR_LAUNCH, "could not read the device status word");
-    return v ? v : w;
+    return v ? v : (w ? w : x);
+}
+
+int moda_depth_proj_append(const ModaTensor* x, const ModaTensor* w, const ModaTensor* k_cache,
+                           const ModaTensor* v_cache, int layer_idx, int num_layers, int seq_len,
+                           int dtype, moda_stream_t stream) {
+    g_err[0] = 0;
+    if (!x || !w || !k_cache || !v_cache) return fail(MODA_ERR_ARG, "null tensor descriptor");
+    if (!dtype_ok(dtype)) return fail(MODA_ERR_DTYPE, "unknown dtype code %d", dtype);
+    if (num_layers <= 0) return fail(MODA_ERR_ARG, "num_layers must be > 0, got %d", num_layers);
+    if (layer_idx < 0 || layer_idx >= num_layers)
+        return fail(MODA_ERR_ARG, "layer_idx %d outside [0, %d)", layer_idx, num_layers);
+    const ModaTensor* all[4] = {x, w, k_cache, v_cache};
+    for (const ModaTensor* t : all)
+        for (int j = 0; j < 4; ++j)
+            if (t->sizes[j] < 0) return fail(MODA_ERR_SHAPE, "negative size");
+    const int64_t B = x->sizes[0], T = x->sizes[2], D = x->sizes[3];
+    const int64_t Hk = k_cache->sizes[1], d = k_cache->sizes[3];
+    if (x->sizes[1] != 1) return fail(MODA_ERR_SHAPE, "x must be [B, 1, T, D]");
+    if (w->sizes[0] != 1 || w->sizes[1] != 1 || w->sizes[2] != 2 * Hk * d || w->sizes[3] != D)
+        return fail(MODA_ERR_SHAPE, "w has shape [%lld,%lld,%lld,%lld], expected [1,1,2*H_k*d = %lld,%lld]",
+                    (long long)w->sizes[0], (long long)w->sizes[1], (long long)w->sizes[2],
+                    (long long)w->sizes[3], (long long)(2 * Hk * d), (long long)D);
+    for (const ModaTensor* c : {k_cache, v_cache}) {
+        if (c->sizes[0] != B || c->sizes[1] != Hk || c->sizes[3] != d)
+            return fail(MODA_ERR_SHAPE, "k_cache and v_cache must both be [B, H_k, rows, d]");
+    }
+    if (seq_len < 0 || seq_len > T) return fail(MODA_ERR_ARG, "seq_len %d outside [0, T = %lld]", seq_len, (long long)T);
+    for (const ModaTensor* c : {k_cache, v_cache})
+        if (c->sizes[2] < static_cast<int64_t>(seq_len) * num_layers)
+            return fail(MODA_ERR_DEPTH_ROWS, "cache has %lld rows < seq_len*L = %lld",
+                        (long long)c->sizes[2], (long long)seq_len * num_layers);
+    if (B > 65535 || T > 0x7fffffff || D > 0x7fffffff || 2 * Hk * d > 0x7fffffff)
+        return fail(MODA_ERR_SHAPE, "sizes too large");
+    for (const ModaTensor* t : all) {
+        int64_t n = 1;
+        for (int j = 0; j < 4; ++j) n *= t->sizes[j];
+        if (n > 0 && !t->ptr) return fail(MODA_ERR_ARG, "null data pointer");
+    }
+    moda::ProjProblem q;
+    q.x = *x;
+    q.w = *w;
+    q.k_cache = *k_cache;
+    q.v_cache = *v_cache;
+    q.B = static_cast<int>(B);
+    q.T = static_cast<int>(T);
+    q.D = static_cast<int>(D);
+    q.N = static_cast<int>(2 * Hk * d);
+    q.Hk = static_cast<int>(Hk);
+    q.d = static_cast<int>(d);
+    q.L = num_layers;
+    q.slot = layer_idx;
+    q.n_write = seq_len;
+    q.dtype = dtype;
+    char why[256];
+    if (!moda::proj_supports(q, why, sizeof(why)))
+        return fail(MODA_ERR_UNSUPPORTED, "fused depth projection %s", why);
+    if (B * Hk * static_cast<int64_t>(seq_len) * d == 0 || D == 0) {
+        if (D == 0 && B * seq_len > 0)
+            return fail(MODA_ERR_UNSUPPORTED, "fused depth projection needs D > 0");
+        return MODA_OK;
+    }
+    cudaGetLastError();
+    char err[256] = "";
+    const int r = moda::launch_proj_append(q, static_cast<cudaStream_t>(stream), err, sizeof(err));
+    if (r != MODA_OK) return fail(r, "%s", err[0] ? err : "projection launch failed");
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(MODA_ERR_LAUNCH, "CUDA launch error: %s", cudaGetErrorString(e));
+    return MODA_OK;
 }
 
 int moda_version(void) { return 200; }

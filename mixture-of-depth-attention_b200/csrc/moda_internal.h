@@ -48,6 +48,27 @@ struct TcParams {
     int zero_rows;  // implicit all-zero depth rows per token (score 0, value 0)
 };
 
+// Depth-write projection with the cache append fused (moda_depth_proj_append):
+// x [B, 1, T, D], w [1, 1, N = 2*H_k*d, D], caches [B, H_k, >= T*L, d].
+struct ProjProblem {
+    ModaTensor x, w, k_cache, v_cache;
+    int B, T, D, N, Hk, d, L, slot, n_write;
+    int dtype;
+};
+
+struct ProjParams {
+    CUtensorMap tm_x, tm_w;  // first: 64-byte aligned
+    void* kc;
+    void* vc;
+    long long kc_sb, kc_sh, kc_sr, vc_sb, vc_sh, vc_sr;  // cache strides (elements)
+    int B, T, K, N, Hk, d, Lc, slot, n_write;
+    int m_tiles_per_batch, n_tiles, num_tiles;
+};
+
+bool proj_supports(const ProjProblem& q, char* why, size_t whylen);
+int launch_proj_append(const ProjProblem& q, cudaStream_t stream, char* err, size_t errlen);
+cudaError_t read_and_clear_proj_status(cudaStream_t stream, int* value);
+
 // TMA map over a [B, H, rows, d] view (128-byte swizzle, box (64, box1, box2, 1)),
 // dimension order (d, H, rows, B) when head_inner (query-like tensors: box (64, G, n)
 // is a token-major tile of G heads x n tokens), else (d, rows, H, B).

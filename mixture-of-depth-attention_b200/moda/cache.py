@@ -11,7 +11,7 @@ from typing import Optional
 import torch
 from torch import Tensor
 
-from .kernels.moda_cuda import depth_append, depth_append_autograd
+from .kernels.moda_cuda import depth_append, depth_append_autograd, depth_proj_append
 
 
 class DepthKVCache:
@@ -81,6 +81,20 @@ class DepthKVCache:
         else:
             depth_append(self.k_cache, self.v_cache, layer_idx, k_depth, v_depth,
                          self.num_layers, T)
+
+    def write_projected(self, layer_idx: int, x: Tensor, w_kv: Tensor,
+                        seq_len: Optional[int] = None):
+        """``write(layer_idx, x @ W_k^T, x @ W_v^T)`` as one kernel: the projection GEMM
+        stores its tiles straight into the cache rows (not in the reference).
+
+        x: [B, T, D]; w_kv: [2*H_k*d, D] = cat(W_k, W_v) (nn.Linear weight layout).
+        No autograd. Raises ``MoDAUnsupported`` before any work for layouts the fused
+        kernel does not take (fp32, head_dim not a multiple of 32, ...).
+        """
+        T = seq_len or x.shape[1]
+        depth_proj_append(x, w_kv, self.k_cache, self.v_cache, layer_idx, self.num_layers, T)
+        self._seq_len = max(self._seq_len, T)
+        self._written = True
 
     def read(self, seq_len: Optional[int] = None) -> tuple[Tensor, Tensor]:
         """Views [B, H_k, T*L, d] of the first T tokens' depth rows (cache.py:76-88)."""

@@ -22,7 +22,7 @@ MODA_ERR_DTYPE, MODA_ERR_LAUNCH, MODA_ERR_UNSUPPORTED = -4, -5, -6
 KERNEL_AUTO, KERNEL_TC, KERNEL_SIMT = 0, 1, 2
 
 EXPORTED_SYMBOLS = ("moda_fwd", "moda_fwd_ex", "moda_fwd_lse", "moda_fwd_zero_depth",
-                    "moda_fwd_plan", "moda_bwd",
+                    "moda_fwd_plan", "moda_bwd", "moda_depth_proj_append",
                     "moda_bwd_noalloc", "moda_bwd_workspace_size", "moda_depth_append",
                     "moda_last_error", "moda_device_status", "moda_version")
 NOALLOC_ROWS = 1 << 20   # MODA_NOALLOC_ROWS
@@ -32,6 +32,11 @@ class ModaTensor(ctypes.Structure):
     _fields_ = [("ptr", ctypes.c_void_p),
                 ("sizes", ctypes.c_int64 * 4),
                 ("strides", ctypes.c_int64 * 4)]
+
+
+class MoDAUnsupported(RuntimeError):
+    """The requested kernel cannot run this dtype / shape / layout (checked on the
+    host before any launch)."""
 
 
 class MoDAShapeError(ValueError, RuntimeError):
@@ -77,6 +82,8 @@ def load():
         lib.moda_fwd_plan.restype = i
         lib.moda_depth_append.argtypes = [T, T, T, T, i, i, i, i, vp]
         lib.moda_depth_append.restype = i
+        lib.moda_depth_proj_append.argtypes = [T, T, T, T, i, i, i, i, vp]
+        lib.moda_depth_proj_append.restype = i
         lib.moda_last_error.argtypes = []
         lib.moda_last_error.restype = ctypes.c_char_p
         lib.moda_device_status.argtypes = [vp]
@@ -107,4 +114,6 @@ def check(code: int, what: str) -> None:
         raise ValueError(msg)
     if code == MODA_ERR_DTYPE:
         raise TypeError(msg)
+    if code == MODA_ERR_UNSUPPORTED:
+        raise MoDAUnsupported(msg)
     raise RuntimeError(msg)

@@ -284,6 +284,34 @@ def depth_append(k_cache: Tensor, v_cache: Tensor, layer_idx: int, k: Tensor, v:
     _lib.check(code, "moda_depth_append")
 
 
+def depth_proj_append(x: Tensor, w_kv: Tensor, k_cache: Tensor, v_cache: Tensor, layer_idx: int,
+                      num_layers: int, seq_len: int) -> None:
+    """k/v depth projections of ``x`` stored straight into the cache rows (one kernel).
+
+    x [B, T, D]; w_kv [2*H_k*d, D] = cat(W_k_depth, W_v_depth); caches [B, H_k, R, d].
+    For t < seq_len: k_cache[:, h, t*L + layer_idx] = (x[:, t] @ W_k_depth.T)[h*d:(h+1)*d],
+    and the same for v. No autograd. Raises ``MoDAUnsupported`` (before any launch) for
+    fp32, d not a multiple of 32, D not a multiple of 8 or unaligned layouts.
+    """
+    for n, t in (("x", x), ("w_kv", w_kv), ("k_cache", k_cache), ("v_cache", v_cache)):
+        if t.device.type != "cuda":
+            raise RuntimeError(f"depth projection runs on CUDA tensors only ({n} is on {t.device})")
+        if t.dtype != x.dtype:
+            raise TypeError(f"{n} has dtype {t.dtype}, x has {x.dtype}")
+    if x.dim() != 3 or w_kv.dim() != 2:
+        raise _lib.MoDAShapeError("x must be [B, T, D] and w_kv [2*H_k*d, D]")
+    if x.dtype not in _DTYPES:
+        raise TypeError(f"unsupported dtype {x.dtype}")
+    lib = _lib.load()
+    stream = torch.cuda.current_stream(x.device).cuda_stream
+    with torch.cuda.device(x.device):
+        code = lib.moda_depth_proj_append(_desc(x.unsqueeze(1)), _desc(w_kv[None, None]),
+                                          _desc(k_cache), _desc(v_cache), int(layer_idx),
+                                          int(num_layers), int(seq_len), _DTYPES[x.dtype],
+                                          stream)
+    _lib.check(code, "moda_depth_proj_append")
+
+
 class _DepthAppendFunction(torch.autograd.Function):
     """In-place depth append that autograd sees, like the reference's strided slice
     assignment into the cache (moda/cache.py:73-74, recorded by torch as a copy into

@@ -23,6 +23,7 @@ from torch import Tensor
 from .config import MoDAConfig
 from .attention import MoDAAttention
 from .cache import DepthKVCache
+from .kernels._lib import MoDAUnsupported
 
 
 def live_write_tokens(seq_len: int, read_layers: int, cache_slots: int, slot: int) -> int:
@@ -36,7 +37,15 @@ def live_write_tokens(seq_len: int, read_layers: int, cache_slots: int, slot: in
 
 
 class MoDATransformerBlock(nn.Module):
-    """MoDAAttention + FFN; both write depth KV (post-norm or pre-norm)."""
+    """MoDAAttention + FFN; both write depth KV (post-norm or pre-norm).
+
+    Without autograd and for 16-bit weights, each depth write -- the attention's (slot
+    2i) and the FFN's (slot 2i+1) -- is one fused kernel: the k/v depth projections with
+    the cache append in the GEMM epilogue (``DepthKVCache.write_projected``). The
+    attention's write still lands after its own attention, as in the reference: with
+    the 2N-slot addressing, layer i's attention reads slot 2i for half of the tokens,
+    and those rows must still be zero then.
+    """
 
     def __init__(self, config: MoDAConfig, layer_idx: int):
         super().__init__()
@@ -54,79 +63,79 @@ class MoDATransformerBlock(nn.Module):
                                           bias=False)
         self.ffn_v_depth_proj = nn.Linear(config.d_model, config.num_kv_heads * config.head_dim,
                                           bias=False)
+        self._kv_weights = {}  # concatenated [W_k; W_v] per projection pair, by weight version
+
+    def _kv_weight(self, k_lin: nn.Linear, v_lin: nn.Linear) -> Tensor:
+        wk, wv = k_lin.weight, v_lin.weight
+        key = (id(k_lin), wk.data_ptr(), wk._version, wv.data_ptr(), wv._version, wk.dtype)
+        hit = self._kv_weights.get(id(k_lin))
+        if hit is None or hit[0] != key:
+            hit = (key, torch.cat([wk, wv]).detach())
+            self._kv_weights[id(k_lin)] = hit
+        return hit[1]
+
+    def _write(self, cache: Optional[DepthKVCache], slot: int, h: Tensor,
+               k_w: Optional[Tensor], v_w: Optional[Tensor], n: int, fuse: bool,
+               k_lin: nn.Linear, v_lin: nn.Linear) -> None:
+        """Cache slot ``slot`` <- depth projections of h for tokens t < n."""
+        if cache is None or n <= 0:
+            return
+        if fuse:
+            try:
+                cache.write_projected(slot, h, self._kv_weight(k_lin, v_lin), seq_len=n)
+                return
+            except MoDAUnsupported:
+                pass  # layout the fused kernel does not take: project, then append
+        B, T, _ = h.shape
+        H_k, d = self.config.num_kv_heads, self.config.head_dim
+        if k_w is None or k_w.shape[2] < n:
+            k_w = k_lin(h).view(B, T, H_k, d).transpose(1, 2)
+            v_w = v_lin(h).view(B, T, H_k, d).transpose(1, 2)
+        cache.write(slot, k_w, v_w, seq_len=n)
 
     def forward(self, x: Tensor, depth_cache: Optional[DepthKVCache] = None) -> Tensor:
-        if self.config.lean_depth_cache and depth_cache is not None:
-            return self._forward_lean(x, depth_cache)
         B, T, D = x.shape
-        H_k = self.config.num_kv_heads
-        d = self.config.head_dim
+        i = self.layer_idx
         K_depth, V_depth = None, None
+        zero_rows = 0
+        n_attn = n_ffn = T
         if depth_cache is not None:
-            K_depth, V_depth = depth_cache.read(seq_len=T)
-
-        if self.config.post_norm:
-            attn_out, k_w, v_w = self.attn(x, K_depth, V_depth)
-            x = self.norm1(x + attn_out)
-            if depth_cache is not None:
-                depth_cache.write(self.layer_idx * 2, k_w, v_w, seq_len=T)
-            x = self.norm2(x + self.ffn(x))
-            if depth_cache is not None:
-                k_f = self.ffn_k_depth_proj(x).view(B, T, H_k, d).transpose(1, 2)
-                v_f = self.ffn_v_depth_proj(x).view(B, T, H_k, d).transpose(1, 2)
-                depth_cache.write(self.layer_idx * 2 + 1, k_f, v_f, seq_len=T)
-        else:
-            attn_out, k_w, v_w = self.attn(self.norm1(x), K_depth, V_depth)
-            x = x + attn_out
-            if depth_cache is not None:
-                depth_cache.write(self.layer_idx * 2, k_w, v_w, seq_len=T)
-            x = x + self.ffn(self.norm2(x))
-            if depth_cache is not None:
-                k_f = self.ffn_k_depth_proj(x).view(B, T, H_k, d).transpose(1, 2)
-                v_f = self.ffn_v_depth_proj(x).view(B, T, H_k, d).transpose(1, 2)
-                depth_cache.write(self.layer_idx * 2 + 1, k_f, v_f, seq_len=T)
-        return x
-
-    def _forward_lean(self, x: Tensor, depth_cache: DepthKVCache) -> Tensor:
-        """The default forward minus cache work whose result no layer reads."""
-        B, T, D = x.shape
-        H_k = self.config.num_kv_heads
-        d = self.config.head_dim
-        n_read = self.attn.num_layers
-        slots = depth_cache.num_layers
-        last = self.layer_idx == self.config.num_layers - 1
-        n_attn = 0 if last else live_write_tokens(T, n_read, slots, 2 * self.layer_idx)
-        n_ffn = 0 if last else live_write_tokens(T, n_read, slots, 2 * self.layer_idx + 1)
-        if depth_cache._written or T * slots == 0:
-            K_depth, V_depth = depth_cache.read(seq_len=T)
-            zero_rows = 0
-        else:  # nothing written yet: every addressed row is zero
-            K_depth = V_depth = None
-            zero_rows = n_read
+            if self.config.lean_depth_cache:
+                # the cache work no layer reads is skipped (see the module docstring)
+                n_read, slots = self.attn.num_layers, depth_cache.num_layers
+                last = i == self.config.num_layers - 1
+                n_attn = 0 if last else live_write_tokens(T, n_read, slots, 2 * i)
+                n_ffn = 0 if last else live_write_tokens(T, n_read, slots, 2 * i + 1)
+            if self.config.lean_depth_cache and not depth_cache._written and \
+                    T * depth_cache.num_layers > 0:
+                zero_rows = self.attn.num_layers  # nothing written yet: all rows are zero
+            else:
+                K_depth, V_depth = depth_cache.read(seq_len=T)
+        fuse = (depth_cache is not None and not torch.is_grad_enabled() and
+                x.dtype in (torch.float16, torch.bfloat16))
+        n_proj = 0 if fuse else (None if n_attn == T else n_attn)
 
         def attend(h):
-            return self.attn(h, K_depth, V_depth, zero_depth_rows=zero_rows, write_tokens=n_attn)
-
-        def write_ffn(h):
-            if n_ffn > 0:  # projected over all T tokens (a token slice would be copied)
-                k_f = self.ffn_k_depth_proj(h).view(B, T, H_k, d).transpose(1, 2)
-                v_f = self.ffn_v_depth_proj(h).view(B, T, H_k, d).transpose(1, 2)
-                depth_cache.write(self.layer_idx * 2 + 1, k_f, v_f, seq_len=n_ffn)
+            return self.attn(h, K_depth, V_depth, zero_depth_rows=zero_rows, write_tokens=n_proj)
 
         if self.config.post_norm:
             attn_out, k_w, v_w = attend(x)
+            h_attn = x
             x = self.norm1(x + attn_out)
-            if n_attn > 0:
-                depth_cache.write(self.layer_idx * 2, k_w, v_w, seq_len=n_attn)
+            self._write(depth_cache, 2 * i, h_attn, k_w, v_w, n_attn, fuse,
+                        self.attn.k_depth_proj, self.attn.v_depth_proj)
             x = self.norm2(x + self.ffn(x))
-            write_ffn(x)
+            self._write(depth_cache, 2 * i + 1, x, None, None, n_ffn, fuse,
+                        self.ffn_k_depth_proj, self.ffn_v_depth_proj)
         else:
-            attn_out, k_w, v_w = attend(self.norm1(x))
+            h_attn = self.norm1(x)
+            attn_out, k_w, v_w = attend(h_attn)
             x = x + attn_out
-            if n_attn > 0:
-                depth_cache.write(self.layer_idx * 2, k_w, v_w, seq_len=n_attn)
+            self._write(depth_cache, 2 * i, h_attn, k_w, v_w, n_attn, fuse,
+                        self.attn.k_depth_proj, self.attn.v_depth_proj)
             x = x + self.ffn(self.norm2(x))
-            write_ffn(x)
+            self._write(depth_cache, 2 * i + 1, x, None, None, n_ffn, fuse,
+                        self.ffn_k_depth_proj, self.ffn_v_depth_proj)
         return x
 
 

@@ -172,3 +172,22 @@ def test_zero_depth_rejects_bad_arguments_before_launch(case):
                                    _lib.MODA_BF16, _lib.KERNEL_AUTO, None)
     assert code == (_lib.MODA_ERR_ARG if case == "negative_rows" else _lib.MODA_ERR_SHAPE)
     assert lib.moda_last_error() != b""
+
+
+@pytest.mark.parametrize("case", ["fp32", "w_rows", "short_cache", "slot"])
+def test_depth_projection_rejects_before_launch(case):
+    lib = _lib.load()
+    dt = torch.float32 if case == "fp32" else torch.bfloat16
+    B, T, D, Hk, d, L = 1, 8, 64, 2, 32, 3
+    x = _t((B, 1, T, D), dt)
+    w = _t((1, 1, 2 * Hk * d + (8 if case == "w_rows" else 0), D), dt)
+    R = T * L - (1 if case == "short_cache" else 0)
+    kc, vc = _t((B, Hk, R, d), dt), _t((B, Hk, R, d), dt)
+    D_ = lambda t: _lib.describe(t.data_ptr(), t.shape, t.stride())
+    code = lib.moda_depth_proj_append(D_(x), D_(w), D_(kc), D_(vc), L if case == "slot" else 1,
+                                      L, T, _lib.MODA_F32 if case == "fp32" else _lib.MODA_BF16,
+                                      None)
+    expect = {"fp32": _lib.MODA_ERR_UNSUPPORTED, "w_rows": _lib.MODA_ERR_SHAPE,
+              "short_cache": _lib.MODA_ERR_DEPTH_ROWS, "slot": _lib.MODA_ERR_ARG}[case]
+    assert code == expect
+    assert lib.moda_last_error() != b""
