@@ -29,6 +29,12 @@ with the reference's cache lifecycle and again with the opt-in lean one.
 cache slot 5 of a [8, 4, 4096*48, 128] cache) against the same work as two library
 GEMMs plus the append kernel; ``--batch`` shrinks B for profiling.
 
+``--pass triton-reference`` (one GPU) times the reference's own GPU path,
+``moda_attention_triton`` (SDPA over repeat_interleave'd K/V plus its Triton depth
+combine kernel), installed unmodified in ``baseline/_ref`` and imported from there under
+a separate package name, on the same inputs as the default workload; it also reports
+the largest difference from this library's output.
+
 ``--pass backward`` (one GPU) times the backward kernels instead: one step = the
 gradients of all five inputs for a seeded dO, from the forward's O and row
 log-sum-exp (computed once, untimed). Its algorithmic FLOPs are 2.5x the
@@ -223,7 +229,8 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="kernel")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--pass", dest="which", choices=["forward", "backward", "model", "proj"],
+    ap.add_argument("--pass", dest="which",
+                    choices=["forward", "backward", "model", "proj", "triton-reference"],
                     default="forward")
     ap.add_argument("--batch", type=int, default=None, help="batch override for --pass proj")
     ap.add_argument("--kernel-shares", action="store_true",
@@ -238,6 +245,8 @@ def main():
         return run_model(args)
     if args.which == "proj":
         return run_proj(args)
+    if args.which == "triton-reference":
+        return run_triton_reference(args, wl)
     args.warmup = max(args.warmup, 3)
 
     import torch
@@ -513,6 +522,69 @@ def run_model(args):
         "verify": {"finite": bool(torch.isfinite(outs[False]).all()),
                    "device_status": device_status(dev)},
     }
+    print(json.dumps(line), flush=True)
+
+
+def load_reference_package():
+    """The reference package from baseline/_ref, imported as ``moda_reference`` (this
+    repository's own package is also called ``moda``)."""
+    import importlib.util
+    root = os.path.join(REPO, "baseline", "_ref", "moda")
+    spec = importlib.util.spec_from_file_location(
+        "moda_reference", os.path.join(root, "__init__.py"), submodule_search_locations=[root])
+    if spec is None or not os.path.exists(os.path.join(root, "__init__.py")):
+        raise ImportError("baseline/_ref/moda is not installed")
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["moda_reference"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def run_triton_reference(args, wl):
+    """The reference's GPU forward (moda_attention_triton) timed on one GPU."""
+    import torch
+    args.warmup = max(args.warmup, 3)
+    B, Hq, Hk, T, d, L, C = wl["B"], wl["Hq"], wl["Hk"], wl["T"], wl["d"], wl["L"], wl["chunk"]
+    base = {"metric": METRIC, "unit": "TFLOP/s", "n_gpus": 1, "impl": "reference-triton-gpu",
+            "higher_is_better": True, "dtype": "bf16", "data": "synthetic N(0,1), seeded per batch",
+            "config": {"workload": wl["desc"]}}
+    try:
+        ref = load_reference_package()
+        triton_fn = ref.kernels.moda_attention_triton
+    except Exception as e:  # noqa: BLE001 -- reported, not hidden
+        print(json.dumps({**base, "unavailable": f"reference Triton path not importable: {e!r}"[:300]}))
+        return
+    from moda.kernels import device_status
+    from moda.kernels.moda_cuda import moda_forward_into
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    Q, K, V, Kd, Vd = make_inputs(wl, 0, B, dev, torch.bfloat16)
+    stream = torch.cuda.current_stream(dev)
+    try:
+        for _ in range(args.warmup):
+            out = triton_fn(Q, K, V, Kd, Vd, num_layers=L, chunk_size=C)
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(0) as clocks:
+            e0.record(stream)
+            for _ in range(args.steps):
+                out = triton_fn(Q, K, V, Kd, Vd, num_layers=L, chunk_size=C)
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+    except Exception as e:  # noqa: BLE001
+        print(json.dumps({**base, "unavailable": f"reference Triton path failed: {e!r}"[:300]}))
+        return
+    ms = e0.elapsed_time(e1) / args.steps
+    ours = torch.empty_like(Q)
+    moda_forward_into(ours, Q, K, V, Kd, Vd, L, None, C)
+    torch.cuda.synchronize(dev)
+    diff = (ours.float() - out.float()).abs().max().item()
+    tflops = flops(B, Hq, T, d, L) / (ms * 1e-3) / 1e12
+    line = {**base, "value": tflops, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms, "scaling": "weak", "vs_baseline": None,
+            "tokens_per_s": B * T / (ms * 1e-3),
+            "max_abs_diff_vs_this_library": diff, "clocks": clocks.summary(),
+            "verify": {"device_status": device_status(dev)}}
     print(json.dumps(line), flush=True)
 
 
