@@ -721,6 +721,299 @@ static bool launch_depth_warp(const BwdParams& p, cudaStream_t stream) {
     }
 }
 
+// ---------------------------------------------------------------- depth part, tensor cores
+// One warp per 16-row block of query rows of one (batch, KV head): 16/G whole tokens
+// (block row r is token t0 + r/G, query head hk*G + r%G). Per token of the block, with
+// its L <= 32 depth rows staged in the warp's shared memory (cp.async):
+//   S = Q Kd^T, dP = dO Vd^T                 16 x 32, mma.sync m16n8k16, fp32 accumulate
+//   P = exp(scale*S - lse), dS = P (dP - D)  the token's own rows; 0 for the others
+//   dQ += scale * dS Kd                      added to the dQ the tcgen05 kernel wrote
+//   dVd = P^T dO, dKd = scale * dS^T Q       32 x d (P and dS go through shared memory)
+// Shared-memory rows of 128 bytes (64 columns) are stored with the 16-byte chunk index
+// XORed with row % 8, so ldmatrix reads of 8 consecutive rows hit 8 different banks.
+// Staging rows past L stay zero (their products must be finite).
+constexpr int kDmWarps = 4;
+
+template <int HD>
+struct DmCfg {
+    static constexpr int kBox16 = 16 * 128;             // 16 rows x 64 columns
+    static constexpr int kBox32 = 32 * 128;             // 32 rows x 64 columns
+    static constexpr int kQ = 0;                         // Q block   [HD/64][16][128 B]
+    static constexpr int kDO = kQ + (HD / 64) * kBox16;  // dO block
+    static constexpr int kK = kDO + (HD / 64) * kBox16;  // K_depth  [HD/64][32][128 B]
+    static constexpr int kV = kK + (HD / 64) * kBox32;   // V_depth
+    static constexpr int kP = kV + (HD / 64) * kBox32;   // P  [16][80 B] (32 keys, padded)
+    static constexpr int kDS = kP + 16 * 80;             // dS
+    static constexpr int kWarp = kDS + 16 * 80;          // bytes per warp
+};
+
+template <int FMT>
+MODA_DEV void dm_mma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    if constexpr (FMT == 1)
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7},"
+            " {%8,%9}, {%0,%1,%2,%3};"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    else
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7},"
+            " {%8,%9}, {%0,%1,%2,%3};"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+MODA_DEV void dm_ldsm(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+}
+MODA_DEV void dm_ldsm_t(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+}
+MODA_DEV uint32_t dm_sw(uint32_t base, int row, int chunk) {
+    return base + row * 128 + (((chunk ^ row) & 7) << 4);
+}
+MODA_DEV void dm_cp16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+MODA_DEV void dm_cp_wait() {
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+template <int FMT>
+MODA_DEV uint32_t dm_pack(float lo, float hi) {
+    return FMT == 1 ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
+}
+template <int FMT>
+MODA_DEV float2 dm_unpack(uint32_t w) {
+    if constexpr (FMT == 1) return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+    return make_float2(__half2float(__ushort_as_half(static_cast<unsigned short>(w & 0xffffu))),
+                       __half2float(__ushort_as_half(static_cast<unsigned short>(w >> 16))));
+}
+
+template <int HD, int FMT>
+__global__ void __launch_bounds__(kDmWarps * 32) moda_bwd_depth_mma_kernel(const __grid_constant__ BwdParams p) {
+    using C = DmCfg<HD>;
+    extern __shared__ __align__(16) uint8_t dm_smem[];
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, c = lane & 3;
+    const uint32_t base = smem_u32(dm_smem) + w * C::kWarp;
+    const int G = p.G, L = p.L, T = p.T, Hk = p.Hk;
+    const int tpg = 16 / G;
+    const long long bpb = (static_cast<long long>(T) * G + 15) / 16;  // 16-row blocks per (b, KV head)
+    const long long nblocks = static_cast<long long>(p.B) * Hk * bpb;
+    const float sc2 = p.scale * kLog2e;
+    for (int i = lane; i < (C::kP - C::kK) / 16; i += 32)
+        asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(base + C::kK + 16 * i), "r"(0u) : "memory");
+    __syncwarp();
+    const uint16_t* q = static_cast<const uint16_t*>(p.q.ptr);
+    const uint16_t* dout = static_cast<const uint16_t*>(p.dout.ptr);
+    const uint16_t* kd = static_cast<const uint16_t*>(p.kd.ptr);
+    const uint16_t* vd = static_cast<const uint16_t*>(p.vd.ptr);
+    uint16_t* dq = static_cast<uint16_t*>(p.dq.ptr);
+    uint16_t* dkd = static_cast<uint16_t*>(p.dkd.ptr);
+    uint16_t* dvd = static_cast<uint16_t*>(p.dvd.ptr);
+    for (long long blk = static_cast<long long>(blockIdx.x) * kDmWarps + w; blk < nblocks;
+         blk += static_cast<long long>(gridDim.x) * kDmWarps) {
+        const int b = static_cast<int>(blk / (Hk * bpb));
+        const int hk = static_cast<int>((blk / bpb) % Hk);
+        const int t0 = static_cast<int>(blk % bpb) * tpg;
+        // ---- stage the block's Q and dO rows
+        for (int i = lane; i < 16 * (HD / 8); i += 32) {
+            const int r = i / (HD / 8), ch = i % (HD / 8);
+            int t = t0 + r / G;
+            if (t >= T) t = t0;  // rows past T read a valid row and are never used
+            const int h = hk * G + r % G;
+            dm_cp16(dm_sw(base + C::kQ + (ch >> 3) * C::kBox16, r, ch & 7),
+                    q + b * p.q.strides[0] + h * p.q.strides[1] + static_cast<long long>(t) * p.q.strides[2] + ch * 8);
+            dm_cp16(dm_sw(base + C::kDO + (ch >> 3) * C::kBox16, r, ch & 7),
+                    dout + b * p.dout.strides[0] + h * p.dout.strides[1] + static_cast<long long>(t) * p.dout.strides[2] + ch * 8);
+        }
+        // this thread's rows of the block: A = g, B = g + 8
+        const int tA = t0 + g / G, tB = t0 + (g + 8) / G;
+        const int hA = hk * G + g % G, hB = hk * G + (g + 8) % G;
+        const bool vA = tA < T, vB = tB < T;
+        const long long riA = (static_cast<long long>(b) * p.Hq + hA) * T + (vA ? tA : t0);
+        const long long riB = (static_cast<long long>(b) * p.Hq + hB) * T + (vB ? tB : t0);
+        const float lseA = p.lse[riA] * kLog2e, lseB = p.lse[riB] * kLog2e;
+        const float dA = p.delta[riA], dB = p.delta[riB];
+        for (int j = 0; j < tpg; ++j) {
+            const int t = t0 + j;
+            if (t >= T) break;
+            const bool ownA = vA && g / G == j, ownB = vB && (g + 8) / G == j;
+            // ---- stage the token's K_depth and V_depth rows
+            const long long row0 = static_cast<long long>(t) * L;
+            for (int i = lane; i < L * (HD / 8); i += 32) {
+                const int l = i / (HD / 8), ch = i % (HD / 8);
+                dm_cp16(dm_sw(base + C::kK + (ch >> 3) * C::kBox32, l, ch & 7),
+                        kd + b * p.kd.strides[0] + hk * p.kd.strides[1] + (row0 + l) * p.kd.strides[2] + ch * 8);
+                dm_cp16(dm_sw(base + C::kV + (ch >> 3) * C::kBox32, l, ch & 7),
+                        vd + b * p.vd.strides[0] + hk * p.vd.strides[1] + (row0 + l) * p.vd.strides[2] + ch * 8);
+            }
+            dm_cp_wait();
+            __syncwarp();
+            // ---- S = Q Kd^T and dP = dO Vd^T
+            float sacc[4][4], pacc[4][4];
+#pragma unroll
+            for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) sacc[nt][e] = pacc[nt][e] = 0.f;
+#pragma unroll
+            for (int ks = 0; ks < HD / 16; ++ks) {
+                uint32_t aq[4], ao[4];
+                dm_ldsm(dm_sw(base + C::kQ + (ks >> 2) * C::kBox16, lane & 15, 2 * (ks & 3) + (lane >> 4)), aq);
+                dm_ldsm(dm_sw(base + C::kDO + (ks >> 2) * C::kBox16, lane & 15, 2 * (ks & 3) + (lane >> 4)), ao);
+#pragma unroll
+                for (int np = 0; np < 2; ++np) {
+                    if (16 * np >= L) break;
+                    const int kr = 16 * np + (lane & 7) + 8 * (lane >> 4);
+                    const int kc = 2 * (ks & 3) + ((lane >> 3) & 1);
+                    uint32_t bk[4], bv[4];
+                    dm_ldsm(dm_sw(base + C::kK + (ks >> 2) * C::kBox32, kr, kc), bk);
+                    dm_ldsm(dm_sw(base + C::kV + (ks >> 2) * C::kBox32, kr, kc), bv);
+                    dm_mma<FMT>(sacc[2 * np], aq, bk[0], bk[1]);
+                    dm_mma<FMT>(sacc[2 * np + 1], aq, bk[2], bk[3]);
+                    dm_mma<FMT>(pacc[2 * np], ao, bv[0], bv[1]);
+                    dm_mma<FMT>(pacc[2 * np + 1], ao, bv[2], bv[3]);
+                }
+            }
+            // ---- P and dS (the token's rows and keys < L only)
+            uint32_t dsf[2][4];  // dS as 16-bit A fragments (keys 16u..16u+15)
+            const uint32_t sP = base + C::kP, sDS = base + C::kDS;
+#pragma unroll
+            for (int nt = 0; nt < 4; ++nt) {
+                float pv[4], dv[4];
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const bool ok = 8 * nt + 2 * c + e < L;
+                    pv[e] = (ownA && ok) ? ex2(fmaf(sacc[nt][e], sc2, -lseA)) : 0.f;
+                    pv[2 + e] = (ownB && ok) ? ex2(fmaf(sacc[nt][2 + e], sc2, -lseB)) : 0.f;
+                    dv[e] = pv[e] * (pacc[nt][e] - dA);
+                    dv[2 + e] = pv[2 + e] * (pacc[nt][2 + e] - dB);
+                }
+                dsf[nt >> 1][(nt & 1) * 2] = dm_pack<FMT>(dv[0], dv[1]);
+                dsf[nt >> 1][(nt & 1) * 2 + 1] = dm_pack<FMT>(dv[2], dv[3]);
+                const int col = 2 * (8 * nt + 2 * c);  // byte offset of keys 8nt + 2c, +1
+                asm volatile("st.shared.u32 [%0], %1;" ::"r"(sP + g * 80 + col), "r"(dm_pack<FMT>(pv[0], pv[1])) : "memory");
+                asm volatile("st.shared.u32 [%0], %1;" ::"r"(sP + (g + 8) * 80 + col), "r"(dm_pack<FMT>(pv[2], pv[3])) : "memory");
+                asm volatile("st.shared.u32 [%0], %1;" ::"r"(sDS + g * 80 + col), "r"(dsf[nt >> 1][(nt & 1) * 2]) : "memory");
+                asm volatile("st.shared.u32 [%0], %1;" ::"r"(sDS + (g + 8) * 80 + col), "r"(dsf[nt >> 1][(nt & 1) * 2 + 1]) : "memory");
+            }
+            __syncwarp();
+            // ---- dQ += scale * dS Kd, 32 columns at a time
+#pragma unroll
+            for (int q4 = 0; q4 < HD / 32; ++q4) {
+                float o[4][4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    if (16 * u >= L) break;
+#pragma unroll
+                    for (int hp = 0; hp < 2; ++hp) {
+                        const int ch = 4 * q4 + 2 * hp + (lane >> 4);
+                        uint32_t bk[4];
+                        dm_ldsm_t(dm_sw(base + C::kK + (ch >> 3) * C::kBox32, 16 * u + (lane & 7) + 8 * ((lane >> 3) & 1), ch & 7), bk);
+                        dm_mma<FMT>(o[2 * hp], dsf[u], bk[0], bk[1]);
+                        dm_mma<FMT>(o[2 * hp + 1], dsf[u], bk[2], bk[3]);
+                    }
+                }
+#pragma unroll
+                for (int rr = 0; rr < 2; ++rr) {
+                    if (!(rr == 0 ? ownA : ownB)) continue;
+                    uint16_t* row = dq + b * p.dq.strides[0] + (rr == 0 ? hA : hB) * p.dq.strides[1] +
+                                    static_cast<long long>(t) * p.dq.strides[2];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        uint32_t* cell = reinterpret_cast<uint32_t*>(row + 8 * (4 * q4 + i) + 2 * c);
+                        const float2 old = dm_unpack<FMT>(*cell);
+                        *cell = dm_pack<FMT>(fmaf(o[i][2 * rr], p.scale, old.x), fmaf(o[i][2 * rr + 1], p.scale, old.y));
+                    }
+                }
+            }
+            // ---- dVd = P^T dO and dKd = scale * dS^T Q, keys 16m..16m+15
+#pragma unroll
+            for (int m = 0; m < 2; ++m) {
+                if (16 * m >= L) break;
+                uint32_t pa[4], da[4];
+                const int ar = (lane & 7) + 8 * (lane >> 4);
+                const int ac = 2 * m + ((lane >> 3) & 1);
+                dm_ldsm_t(sP + ar * 80 + ac * 16, pa);
+                dm_ldsm_t(sDS + ar * 80 + ac * 16, da);
+#pragma unroll
+                for (int q4 = 0; q4 < HD / 32; ++q4) {
+                    float ov[4][4], ok[4][4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) ov[i][e] = ok[i][e] = 0.f;
+#pragma unroll
+                    for (int hp = 0; hp < 2; ++hp) {
+                        const int ch = 4 * q4 + 2 * hp + (lane >> 4);
+                        const int br = (lane & 7) + 8 * ((lane >> 3) & 1);
+                        uint32_t bo[4], bq[4];
+                        dm_ldsm_t(dm_sw(base + C::kDO + (ch >> 3) * C::kBox16, br, ch & 7), bo);
+                        dm_ldsm_t(dm_sw(base + C::kQ + (ch >> 3) * C::kBox16, br, ch & 7), bq);
+                        dm_mma<FMT>(ov[2 * hp], pa, bo[0], bo[1]);
+                        dm_mma<FMT>(ov[2 * hp + 1], pa, bo[2], bo[3]);
+                        dm_mma<FMT>(ok[2 * hp], da, bq[0], bq[1]);
+                        dm_mma<FMT>(ok[2 * hp + 1], da, bq[2], bq[3]);
+                    }
+                    // ov / ok [i]: keys 16m + g (0,1) and 16m + g + 8 (2,3), columns 8(4q4+i) + 2c, +1
+#pragma unroll
+                    for (int kk = 0; kk < 2; ++kk) {
+                        const int key = 16 * m + g + 8 * kk;
+                        if (key >= L) continue;
+                        uint16_t* vrow = dvd + b * p.dvd.strides[0] + hk * p.dvd.strides[1] + (row0 + key) * p.dvd.strides[2];
+                        uint16_t* krow = dkd + b * p.dkd.strides[0] + hk * p.dkd.strides[1] + (row0 + key) * p.dkd.strides[2];
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const int col = 8 * (4 * q4 + i) + 2 * c;
+                            *reinterpret_cast<uint32_t*>(vrow + col) = dm_pack<FMT>(ov[i][2 * kk], ov[i][2 * kk + 1]);
+                            *reinterpret_cast<uint32_t*>(krow + col) =
+                                dm_pack<FMT>(ok[i][2 * kk] * p.scale, ok[i][2 * kk + 1] * p.scale);
+                        }
+                    }
+                }
+            }
+            __syncwarp();  // every lane is done with this token's staging before the next copies
+        }
+        __syncwarp();  // and with the block's Q / dO before the next block's copies
+    }
+}
+
+template <int HD>
+static bool launch_depth_mma_hd(const BwdParams& p, cudaStream_t stream) {
+    using C = DmCfg<HD>;
+    const long long bpb = (static_cast<long long>(p.T) * p.G + 15) / 16;
+    const long long n = static_cast<long long>(p.B) * p.Hk * bpb;
+    const long long want = (n + kDmWarps - 1) / kDmWarps;
+    const int grid = static_cast<int>(want < 2LL * sm_count() ? want : 2LL * sm_count());
+    const int smem = kDmWarps * C::kWarp;
+    auto launch = [&](auto kern) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+            return false;
+        kern<<<grid, kDmWarps * 32, smem, stream>>>(p);
+        return true;
+    };
+    return p.dtype == MODA_BF16 ? launch(moda_bwd_depth_mma_kernel<HD, 1>) : launch(moda_bwd_depth_mma_kernel<HD, 0>);
+}
+
+// The tensor-core depth kernel for 16-bit inputs with d in {64, 128}, whole tokens per
+// 16-row block (16 % G == 0), L <= 32 and 16-byte aligned unit-stride rows.
+static bool launch_depth_mma(const BwdParams& p, cudaStream_t stream) {
+    if (p.dtype != MODA_BF16 && p.dtype != MODA_F16) return false;
+    if (p.L < 1 || p.L > 32 || p.G < 1 || 16 % p.G != 0) return false;
+    const ModaTensor* ts[7] = {&p.q, &p.dout, &p.kd, &p.vd, &p.dkd, &p.dvd, &p.dq};
+    for (const ModaTensor* x : ts) {
+        if (x->strides[3] != 1 || reinterpret_cast<uintptr_t>(x->ptr) % 16 != 0) return false;
+        for (int i = 0; i < 3; ++i)
+            if (x->sizes[i] > 1 && (x->strides[i] * 2) % 16 != 0) return false;
+    }
+    if (p.d == 128) return launch_depth_mma_hd<128>(p, stream);
+    if (p.d == 64) return launch_depth_mma_hd<64>(p, stream);
+    return false;
+}
+
 // Zero gradient for depth rows the forward never reads (rows >= T*L).
 template <typename T>
 __global__ void moda_bwd_zero_rows_kernel(const __grid_constant__ BwdParams p, long long r_lo) {
@@ -740,7 +1033,7 @@ size_t depth_token_smem(int G, int L, int d) {
 
 template <typename T>
 static int launch_depth_t(const BwdParams& p, cudaStream_t stream) {
-    if (p.L > 0 && p.T > 0 && !launch_depth_warp<T>(p, stream)) {
+    if (p.L > 0 && p.T > 0 && !launch_depth_mma(p, stream) && !launch_depth_warp<T>(p, stream)) {
         const size_t sm = depth_token_smem(p.G, p.L, p.d);
         if (sm > 48 * 1024 &&
             cudaFuncSetAttribute(moda_bwd_depth_token_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,

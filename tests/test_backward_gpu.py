@@ -168,3 +168,27 @@ def test_model_gradients_match_reference(name, lean):
         else:
             assert p.grad is not None, pname
             assert rel_err(p.grad.cpu().numpy(), z["g." + pname]) <= FP32_REL_TOL, pname
+
+
+DEPTH_MMA_CASES = [  # B, H_q, H_k, T, d, L: the tensor-core depth backward's range
+    (1, 8, 2, 37, 128, 32),   # G = 4, L at its maximum, T ends inside a 16-row block
+    (1, 16, 2, 20, 64, 17),   # G = 8, L not a multiple of 8
+    (2, 16, 1, 9, 128, 5),    # G = 16: one token per block
+    (1, 2, 2, 33, 64, 32),    # G = 1: sixteen tokens per block
+]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "f16"])
+@pytest.mark.parametrize("case", DEPTH_MMA_CASES, ids=[str(c) for c in DEPTH_MMA_CASES])
+def test_depth_backward_tensor_core_range(case, dtype):
+    B, Hq, Hk, T, d, L = case
+    arrs = seeded_inputs(B, Hq, Hk, T, d, L, seed=60 + T)
+    dO = np.random.default_rng(61 + T).standard_normal((B, Hq, T, d)).astype(np.float32)
+    rin = rounded(arrs + [dO], dtype)
+    ref = orc.moda_attention_grads(*rin[:5], L, rin[5])
+    ins = dev(arrs, dtype)
+    O, lse = moda_forward_lse(*ins, L)
+    grads = moda_backward(dev([dO], dtype)[0], *ins, O, lse, L)
+    torch.cuda.synchronize()
+    for g, k in zip(grads, GRADS):
+        assert half_ok(host(g), ref[k]), (k, float(np.max(np.abs(host(g) - ref[k]))))
