@@ -724,14 +724,15 @@ static bool launch_depth_warp(const BwdParams& p, cudaStream_t stream) {
 // ---------------------------------------------------------------- depth part, tensor cores
 // One warp per 16-row block of query rows of one (batch, KV head): 16/G whole tokens
 // (block row r is token t0 + r/G, query head hk*G + r%G). Per token of the block, with
-// its L <= 32 depth rows staged in the warp's shared memory (cp.async):
+// its depth rows staged in the warp's shared memory (cp.async) 32 at a time (P uses the
+// forward's log-sum-exp, so key chunks are independent):
 //   S = Q Kd^T, dP = dO Vd^T                 16 x 32, mma.sync m16n8k16, fp32 accumulate
 //   P = exp(scale*S - lse), dS = P (dP - D)  the token's own rows; 0 for the others
 //   dQ += scale * dS Kd                      added to the dQ the tcgen05 kernel wrote
 //   dVd = P^T dO, dKd = scale * dS^T Q       32 x d (P and dS go through shared memory)
 // Shared-memory rows of 128 bytes (64 columns) are stored with the 16-byte chunk index
 // XORed with row % 8, so ldmatrix reads of 8 consecutive rows hit 8 different banks.
-// Staging rows past L stay zero (their products must be finite).
+// Staging rows past a partial chunk are zeroed (their products must be finite).
 constexpr int kDmWarps = 4;
 
 template <int HD>
@@ -836,13 +837,23 @@ __global__ void __launch_bounds__(kDmWarps * 32) moda_bwd_depth_mma_kernel(const
         const long long riB = (static_cast<long long>(b) * p.Hq + hB) * T + (vB ? tB : t0);
         const float lseA = p.lse[riA] * kLog2e, lseB = p.lse[riB] * kLog2e;
         const float dA = p.delta[riA], dB = p.delta[riB];
-        for (int j = 0; j < tpg; ++j) {
+        for (int jc = 0; jc < tpg * ((L + 31) / 32); ++jc) {
+            const int j = jc / ((L + 31) / 32);            // token of the block
+            const int kc = 32 * (jc % ((L + 31) / 32));    // first depth row of the chunk
             const int t = t0 + j;
             if (t >= T) break;
+            const int Lc = L - kc < 32 ? L - kc : 32;      // rows in this chunk
             const bool ownA = vA && g / G == j, ownB = vB && (g + 8) / G == j;
-            // ---- stage the token's K_depth and V_depth rows
-            const long long row0 = static_cast<long long>(t) * L;
-            for (int i = lane; i < L * (HD / 8); i += 32) {
+            // ---- stage the chunk's K_depth and V_depth rows (rows past Lc zeroed)
+            const long long row0 = static_cast<long long>(t) * L + kc;
+            if (Lc < 32) {
+                for (int i = lane; i < (32 - Lc) * (HD / 8); i += 32) {
+                    const int l = Lc + i / (HD / 8), ch = i % (HD / 8);
+                    asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(dm_sw(base + C::kK + (ch >> 3) * C::kBox32, l, ch & 7)), "r"(0u) : "memory");
+                    asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(dm_sw(base + C::kV + (ch >> 3) * C::kBox32, l, ch & 7)), "r"(0u) : "memory");
+                }
+            }
+            for (int i = lane; i < Lc * (HD / 8); i += 32) {
                 const int l = i / (HD / 8), ch = i % (HD / 8);
                 dm_cp16(dm_sw(base + C::kK + (ch >> 3) * C::kBox32, l, ch & 7),
                         kd + b * p.kd.strides[0] + hk * p.kd.strides[1] + (row0 + l) * p.kd.strides[2] + ch * 8);
@@ -864,7 +875,7 @@ __global__ void __launch_bounds__(kDmWarps * 32) moda_bwd_depth_mma_kernel(const
                 dm_ldsm(dm_sw(base + C::kDO + (ks >> 2) * C::kBox16, lane & 15, 2 * (ks & 3) + (lane >> 4)), ao);
 #pragma unroll
                 for (int np = 0; np < 2; ++np) {
-                    if (16 * np >= L) break;
+                    if (16 * np >= Lc) break;
                     const int kr = 16 * np + (lane & 7) + 8 * (lane >> 4);
                     const int kc = 2 * (ks & 3) + ((lane >> 3) & 1);
                     uint32_t bk[4], bv[4];
@@ -884,11 +895,11 @@ __global__ void __launch_bounds__(kDmWarps * 32) moda_bwd_depth_mma_kernel(const
                 float pv[4], dv[4];
 #pragma unroll
                 for (int e = 0; e < 2; ++e) {
-                    const bool ok = 8 * nt + 2 * c + e < L;
+                    const bool ok = 8 * nt + 2 * c + e < Lc;
                     pv[e] = (ownA && ok) ? ex2(fmaf(sacc[nt][e], sc2, -lseA)) : 0.f;
                     pv[2 + e] = (ownB && ok) ? ex2(fmaf(sacc[nt][2 + e], sc2, -lseB)) : 0.f;
-                    dv[e] = pv[e] * (pacc[nt][e] - dA);
-                    dv[2 + e] = pv[2 + e] * (pacc[nt][2 + e] - dB);
+                    dv[e] = (ownA && ok) ? pv[e] * (pacc[nt][e] - dA) : 0.f;
+                    dv[2 + e] = (ownB && ok) ? pv[2 + e] * (pacc[nt][2 + e] - dB) : 0.f;
                 }
                 dsf[nt >> 1][(nt & 1) * 2] = dm_pack<FMT>(dv[0], dv[1]);
                 dsf[nt >> 1][(nt & 1) * 2 + 1] = dm_pack<FMT>(dv[2], dv[3]);
@@ -907,7 +918,7 @@ __global__ void __launch_bounds__(kDmWarps * 32) moda_bwd_depth_mma_kernel(const
                 for (int i = 0; i < 4; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
 #pragma unroll
                 for (int u = 0; u < 2; ++u) {
-                    if (16 * u >= L) break;
+                    if (16 * u >= Lc) break;
 #pragma unroll
                     for (int hp = 0; hp < 2; ++hp) {
                         const int ch = 4 * q4 + 2 * hp + (lane >> 4);
@@ -933,7 +944,7 @@ __global__ void __launch_bounds__(kDmWarps * 32) moda_bwd_depth_mma_kernel(const
             // ---- dVd = P^T dO and dKd = scale * dS^T Q, keys 16m..16m+15
 #pragma unroll
             for (int m = 0; m < 2; ++m) {
-                if (16 * m >= L) break;
+                if (16 * m >= Lc) break;
                 uint32_t pa[4], da[4];
                 const int ar = (lane & 7) + 8 * (lane >> 4);
                 const int ac = 2 * m + ((lane >> 3) & 1);
@@ -962,7 +973,7 @@ __global__ void __launch_bounds__(kDmWarps * 32) moda_bwd_depth_mma_kernel(const
 #pragma unroll
                     for (int kk = 0; kk < 2; ++kk) {
                         const int key = 16 * m + g + 8 * kk;
-                        if (key >= L) continue;
+                        if (key >= Lc) continue;
                         uint16_t* vrow = dvd + b * p.dvd.strides[0] + hk * p.dvd.strides[1] + (row0 + key) * p.dvd.strides[2];
                         uint16_t* krow = dkd + b * p.dkd.strides[0] + hk * p.dkd.strides[1] + (row0 + key) * p.dkd.strides[2];
 #pragma unroll
@@ -999,10 +1010,10 @@ static bool launch_depth_mma_hd(const BwdParams& p, cudaStream_t stream) {
 }
 
 // The tensor-core depth kernel for 16-bit inputs with d in {64, 128}, whole tokens per
-// 16-row block (16 % G == 0), L <= 32 and 16-byte aligned unit-stride rows.
+// 16-row block (16 % G == 0) and 16-byte aligned unit-stride rows; any L.
 static bool launch_depth_mma(const BwdParams& p, cudaStream_t stream) {
     if (p.dtype != MODA_BF16 && p.dtype != MODA_F16) return false;
-    if (p.L < 1 || p.L > 32 || p.G < 1 || 16 % p.G != 0) return false;
+    if (p.L < 1 || p.G < 1 || 16 % p.G != 0) return false;
     const ModaTensor* ts[7] = {&p.q, &p.dout, &p.kd, &p.vd, &p.dkd, &p.dvd, &p.dq};
     for (const ModaTensor* x : ts) {
         if (x->strides[3] != 1 || reinterpret_cast<uintptr_t>(x->ptr) % 16 != 0) return false;

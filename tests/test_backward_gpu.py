@@ -175,6 +175,8 @@ DEPTH_MMA_CASES = [  # B, H_q, H_k, T, d, L: the tensor-core depth backward's ra
     (1, 16, 2, 20, 64, 17),   # G = 8, L not a multiple of 8
     (2, 16, 1, 9, 128, 5),    # G = 16: one token per block
     (1, 2, 2, 33, 64, 32),    # G = 1: sixteen tokens per block
+    (1, 8, 2, 21, 128, 48),   # two key chunks per token, the second partial
+    (1, 4, 1, 10, 64, 70),    # three key chunks
 ]
 
 
