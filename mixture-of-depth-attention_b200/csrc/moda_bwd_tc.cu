@@ -50,8 +50,9 @@ struct BwdCfg {
     static constexpr int kRingOff = 2 * kTile;
     static constexpr int kStageOff = kRingOff + kStages * 2 * kTile;   // lse/D staging
     static constexpr int kBarOff = kStageOff + 2 * 2 * kBRows * 4;
-    // res_full res_empty st_full pd_full acc_done acc_free end stage, ring_full[S] ring_empty[S]
-    static constexpr int kNumBars = 8 + 2 * kStages;
+    // res_full res_empty st_full_a pd_full_a acc_done acc_free end stage, ring_full[S]
+    // ring_empty[S], st_full_b pd_full_b (a / b: the score tile's column halves)
+    static constexpr int kNumBars = 10 + 2 * kStages;
     static constexpr int kMiscOff = kBarOff + kNumBars * 8;
     static constexpr int kSmem = kMiscOff + 32 + 1024;
     static constexpr uint32_t kTmemCols = 512;
@@ -123,6 +124,9 @@ __global__ void __launch_bounds__(kBThreads, 1) moda_bwd_tc_kernel(const __grid_
     const uint32_t stage_bar = bar0 + 56;
     auto ring_full = [&](uint32_t i) { return bar0 + 8u * (8 + i); };
     auto ring_empty = [&](uint32_t i) { return bar0 + 8u * (8 + Cfg::kStages + i); };
+    // per column half h of the 128-column score tiles: scores ready / P and dS written
+    auto st_full_h = [&](int h) { return h == 0 ? st_full : bar0 + 8u * (8 + 2 * Cfg::kStages); };
+    auto pd_full_h = [&](int h) { return h == 0 ? pd_full : bar0 + 8u * (9 + 2 * Cfg::kStages); };
     float* stage = reinterpret_cast<float*>(smem + Cfg::kStageOff);  // [2][2][128]: lse2, D
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + Cfg::kMiscOff);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Cfg::kMiscOff + 8);
@@ -134,6 +138,8 @@ __global__ void __launch_bounds__(kBThreads, 1) moda_bwd_tc_kernel(const __grid_
         mbar_init(res_empty, 1);
         mbar_init(st_full, 1);
         mbar_init(pd_full, 4);
+        mbar_init(st_full_h(1), 1);
+        mbar_init(pd_full_h(1), 4);
         mbar_init(acc_done, 1);
         mbar_init(acc_free, 4);
         mbar_init(end_bar, 1);
@@ -207,62 +213,100 @@ __global__ void __launch_bounds__(kBThreads, 1) moda_bwd_tc_kernel(const __grid_
     } else if (warp == kWarpMma) {
         if (lane == 0) {
             // ------------------------------------------------------------ MMA issuer
-            constexpr uint32_t idesc_s = make_idesc(FMT, kBRows, kBRows, 0);  // B K-major (d)
-            constexpr uint32_t idesc_o = make_idesc(FMT, kBRows, HD, 1);      // B MN-major (d)
+            // Every step's 128-column score tiles are computed in two column halves (64
+            // ring rows each). Issue order per step s:
+            //   [S, dP half a(s); half b(s) -- issued during step s-1, or at item start]
+            //   dV/dK (dQ) half a(s) once its P / dS are written
+            //   S, dP half a(s+1): overwrite half a's columns after the MMAs above read them
+            //   dV/dK (dQ) half b(s), then S, dP half b(s+1)
+            // so the elementwise work on one half overlaps the tensor core on the other.
+            constexpr uint32_t idesc_h = make_idesc(FMT, kBRows, kBRows / 2, 0);  // B K-major (d)
+            constexpr uint32_t idesc_o = make_idesc(FMT, kBRows, HD, 1);         // B MN-major (d)
             constexpr uint32_t hi = desc_hi_sw128(1024);
             const uint32_t a0 = desc_lo(sRes, 16), a1 = desc_lo(sRes + kTile, 16);
             const uint32_t tS = tmem, tP = tmem + 128;
             uint32_t f = 0, nres = 0, nst = 0, nitems = 0;
             bool ok = true;
+            // S (S^T) = res0 . ring0^T and dP (dP^T) = res1 . ring1^T for ring rows
+            // [64h, 64h + 64), contraction over d, into score columns [64h, 64h + 64)
+            auto issue_scores = [&](uint32_t rb, int h) {
+                const uint32_t b0 = desc_lo(rb + h * 8192, 16), b1 = desc_lo(rb + kTile + h * 8192, 16);
+#pragma unroll
+                for (int kk = 0; kk < HD / 16; ++kk) {
+                    const uint32_t off = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
+                    mma_ss(tS + 64 * h, desc_join(a0 + off, hi), desc_join(b0 + off, hi), idesc_h, kk > 0);
+                }
+#pragma unroll
+                for (int kk = 0; kk < HD / 16; ++kk) {
+                    const uint32_t off = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
+                    mma_ss(tP + 64 * h, desc_join(a1 + off, hi), desc_join(b1 + off, hi), idesc_h, kk > 0);
+                }
+                mma_commit(st_full_h(h));
+            };
+            // contraction over ring rows [64h, 64h + 64) (MN-major B, d contiguous); the
+            // 16-bit P / dS of half h sit in score columns [64h, 64h + 32)
+            auto issue_acc = [&](uint32_t rb, int h, bool first) {
+                const uint32_t v0 = desc_lo(rb, 16384), v1 = desc_lo(rb + kTile, 16384);
+                if (MODE == MODE_DKDV) {
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)   // dV += P^T . dO
+                        mma_ts(tmem + Cfg::kAcc0, tS + 64 * h + kk * 8,
+                               desc_join(v1 + (((4 * h + kk) * 2048) >> 4), hi), idesc_o, (first && kk == 0) ? 0u : 1u);
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)   // dK += dS^T . Q
+                        mma_ts(tmem + Cfg::kAcc1, tP + 64 * h + kk * 8,
+                               desc_join(v0 + (((4 * h + kk) * 2048) >> 4), hi), idesc_o, (first && kk == 0) ? 0u : 1u);
+                } else {
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)   // dQ += dS . K
+                        mma_ts(tmem + Cfg::kAcc0, tS + 64 * h + kk * 8,
+                               desc_join(v0 + (((4 * h + kk) * 2048) >> 4), hi), idesc_o, (first && kk == 0) ? 0u : 1u);
+                }
+            };
             for (int item = blockIdx.x; item < p.num_items && ok; item += gridDim.x) {
                 const BwdItem it = bwd_item<MODE>(p, item);
                 ok = bwait(res_full, nres & 1u, abort_flag, 3);
                 if (!ok) break;
                 ++nres;
+                // the item's first step: both score halves
+                ok = bwait(ring_full(f % Cfg::kStages), (f / Cfg::kStages) & 1u, abort_flag, 4);
+                if (!ok) break;
+                tc_fence_after();
+                {
+                    const uint32_t rb = sRing + (f % Cfg::kStages) * 2 * kTile;
+                    issue_scores(rb, 0);
+                    issue_scores(rb, 1);
+                    if (it.nsteps == 1) mma_commit(res_empty);  // resident tiles no longer read
+                }
                 for (int s = 0; s < it.nsteps; ++s) {
                     const uint32_t slot = f % Cfg::kStages;
                     const uint32_t rb = sRing + slot * 2 * kTile;
-                    ok = bwait(ring_full(slot), (f / Cfg::kStages) & 1u, abort_flag, 4);
-                    if (!ok) break;
-                    tc_fence_after();
-                    // S (S^T) = res0 . ring0^T and dP (dP^T) = res1 . ring1^T, contraction over d
-                    const uint32_t b0 = desc_lo(rb, 16), b1 = desc_lo(rb + kTile, 16);
-#pragma unroll
-                    for (int kk = 0; kk < HD / 16; ++kk) {
-                        const uint32_t off = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
-                        mma_ss(tS, desc_join(a0 + off, hi), desc_join(b0 + off, hi), idesc_s, kk > 0);
-                    }
-#pragma unroll
-                    for (int kk = 0; kk < HD / 16; ++kk) {
-                        const uint32_t off = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
-                        mma_ss(tP, desc_join(a1 + off, hi), desc_join(b1 + off, hi), idesc_s, kk > 0);
-                    }
-                    mma_commit(st_full);
-                    if (s == it.nsteps - 1) mma_commit(res_empty);  // resident tiles no longer read
-                    ok = bwait(pd_full, nst & 1u, abort_flag, 5);
-                    ++nst;
+                    const bool has_next = s + 1 < it.nsteps;
+                    const uint32_t rb_next = sRing + ((f + 1) % Cfg::kStages) * 2 * kTile;
+                    // half a of step s
+                    ok = bwait(pd_full_h(0), nst & 1u, abort_flag, 5);
                     if (ok && s == 0 && nitems > 0) ok = bwait(acc_free, (nitems - 1) & 1u, abort_flag, 6);
                     if (!ok) break;
                     tc_fence_after();
-                    // contraction over the 128 rows of the ring tiles (MN-major B, d contiguous)
-                    const uint32_t v0 = desc_lo(rb, 16384), v1 = desc_lo(rb + kTile, 16384);
-                    if (MODE == MODE_DKDV) {
-#pragma unroll
-                        for (int kk = 0; kk < kBRows / 16; ++kk)   // dV += P^T . dO
-                            mma_ts(tmem + Cfg::kAcc0, tS + kk * 8, desc_join(v1 + ((kk * 2048) >> 4), hi),
-                                   idesc_o, (s == 0 && kk == 0) ? 0u : 1u);
-#pragma unroll
-                        for (int kk = 0; kk < kBRows / 16; ++kk)   // dK += dS^T . Q
-                            mma_ts(tmem + Cfg::kAcc1, tP + kk * 8, desc_join(v0 + ((kk * 2048) >> 4), hi),
-                                   idesc_o, (s == 0 && kk == 0) ? 0u : 1u);
-                    } else {
-#pragma unroll
-                        for (int kk = 0; kk < kBRows / 16; ++kk)   // dQ += dS . K
-                            mma_ts(tmem + Cfg::kAcc0, tS + kk * 8, desc_join(v0 + ((kk * 2048) >> 4), hi),
-                                   idesc_o, (s == 0 && kk == 0) ? 0u : 1u);
+                    issue_acc(rb, 0, s == 0);
+                    if (has_next) {
+                        ok = bwait(ring_full((f + 1) % Cfg::kStages), ((f + 1) / Cfg::kStages) & 1u, abort_flag, 4);
+                        if (!ok) break;
+                        tc_fence_after();
+                        issue_scores(rb_next, 0);
                     }
+                    // half b of step s
+                    ok = bwait(pd_full_h(1), nst & 1u, abort_flag, 5);
+                    if (!ok) break;
+                    ++nst;
+                    tc_fence_after();
+                    issue_acc(rb, 1, false);
                     mma_commit(ring_empty(slot));
-                    if (s == it.nsteps - 1) mma_commit(acc_done);
+                    if (!has_next) mma_commit(acc_done);
+                    if (has_next) {
+                        issue_scores(rb_next, 1);
+                        if (s + 2 == it.nsteps) mma_commit(res_empty);  // last scores of the item
+                    }
                     ++f;
                 }
                 ++nitems;
@@ -322,53 +366,58 @@ __global__ void __launch_bounds__(kBThreads, 1) moda_bwd_tc_kernel(const __grid_
                     col0 = idx * kBRows;
                     need_mask = col0 + kBRows - 1 > it.res0;  // some key above some token
                 }
-                if (!bwait(st_full, nst & 1u, abort_flag, 7)) { ok = false; break; }
-                tc_fence_after();
 #pragma unroll 1
-                for (int c = 0; c < 4; ++c) {
-                    uint32_t sv[32], dv[32];
-                    tmem_ld32(tS + 32 * c, sv);
-                    tmem_ld32(tP + 32 * c, dv);
-                    tmem_wait_ld();
-                    tmem_reg_fence(sv);
-                    tmem_reg_fence(dv);
-                    uint32_t pk_p[16], pk_d[16];
+                for (int h = 0; h < 2 && ok; ++h) {  // the two column halves of the score tiles
+                    if (!bwait(st_full_h(h), nst & 1u, abort_flag, 7)) { ok = false; break; }
+                    tc_fence_after();
+#pragma unroll 1
+                    for (int c = 2 * h; c < 2 * h + 2; ++c) {
+                        uint32_t sv[32], dv[32];
+                        tmem_ld32(tS + 32 * c, sv);
+                        tmem_ld32(tP + 32 * c, dv);
+                        tmem_wait_ld();
+                        tmem_reg_fence(sv);
+                        tmem_reg_fence(dv);
+                        uint32_t pk_p[16], pk_d[16];
 #pragma unroll
-                    for (int i = 0; i < 32; i += 2) {
-                        float pr[2], ds[2];
+                        for (int i = 0; i < 32; i += 2) {
+                            float pr[2], ds[2];
 #pragma unroll
-                        for (int u = 0; u < 2; ++u) {
-                            const int col = 32 * c + i + u;
-                            float l2, dd;
-                            bool valid;
-                            if (MODE == MODE_DKDV) {
-                                l2 = st_lse[col];
-                                dd = st_D[col];
-                                valid = !need_mask || col0 + (col >> gsh) >= key_r;
-                            } else {
-                                l2 = lse2_r;
-                                dd = D_r;
-                                valid = !need_mask || col0 + col <= tok_r;
+                            for (int u = 0; u < 2; ++u) {
+                                const int col = 32 * c + i + u;
+                                float l2, dd;
+                                bool valid;
+                                if (MODE == MODE_DKDV) {
+                                    l2 = st_lse[col];
+                                    dd = st_D[col];
+                                    valid = !need_mask || col0 + (col >> gsh) >= key_r;
+                                } else {
+                                    l2 = lse2_r;
+                                    dd = D_r;
+                                    valid = !need_mask || col0 + col <= tok_r;
+                                }
+                                const float e = ex2(fmaf(__uint_as_float(sv[i + u]), sc2, -l2));
+                                pr[u] = valid ? e : 0.f;
+                                ds[u] = pr[u] * (__uint_as_float(dv[i + u]) - dd);
                             }
-                            const float e = ex2(fmaf(__uint_as_float(sv[i + u]), sc2, -l2));
-                            pr[u] = valid ? e : 0.f;
-                            ds[u] = pr[u] * (__uint_as_float(dv[i + u]) - dd);
+                            pk_p[i >> 1] = FMT == 1 ? pack_bf16x2(pr[0], pr[1]) : pack_f16x2(pr[0], pr[1]);
+                            pk_d[i >> 1] = FMT == 1 ? pack_bf16x2(ds[0], ds[1]) : pack_f16x2(ds[0], ds[1]);
                         }
-                        pk_p[i >> 1] = FMT == 1 ? pack_bf16x2(pr[0], pr[1]) : pack_f16x2(pr[0], pr[1]);
-                        pk_d[i >> 1] = FMT == 1 ? pack_bf16x2(ds[0], ds[1]) : pack_f16x2(ds[0], ds[1]);
+                        // 16-bit results: half h's columns [64h, 64h + 32), already read
+                        const uint32_t poff = 64 * h + 16 * (c - 2 * h);
+                        if (MODE == MODE_DKDV) {
+                            tmem_st16(tS + poff, pk_p);   // P^T
+                            tmem_st16(tP + poff, pk_d);   // dS^T
+                        } else {
+                            tmem_st16(tS + poff, pk_d);   // dS
+                        }
                     }
-                    // 16-bit results go into columns this thread has already read
-                    if (MODE == MODE_DKDV) {
-                        tmem_st16(tS + 16 * c, pk_p);   // P^T
-                        tmem_st16(tP + 16 * c, pk_d);   // dS^T
-                    } else {
-                        tmem_st16(tS + 16 * c, pk_d);   // dS
-                    }
+                    tmem_wait_st();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(pd_full_h(h));
                 }
-                tmem_wait_st();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(pd_full);
+                if (!ok) break;
                 ++nst;
             }
             if (!ok) break;
