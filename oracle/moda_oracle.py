@@ -153,6 +153,36 @@ def moda_row(q, k, v, kd, vd, scale):
     return w[:n] @ v + w[n:] @ vd
 
 
+def moda_token_grads(q, do, k, v, kd, vd, scale):
+    """Exact gradients that one token's G query rows produce, for full-size spot checks.
+
+    q, do [G, d] (the token's query rows and upstream gradients); k, v [t+1, d] (keys
+    0..t of its KV head); kd, vd [L, d] (its own depth rows). Per row, the autograd of
+    the row softmax of moda_naive.py:85-95: w = softmax(scale*[k@q, kd@q]),
+    o = w@[v; vd], D = do.o, ds = w*([v@do, vd@do] - D). Returns dQ [G, d] (complete:
+    a query row depends only on its own keys), and dK_depth, dV_depth [L, d] (complete:
+    a token's depth rows are read only by its own G rows). float64.
+    """
+    q = np.asarray(q, dtype=np.float64)
+    do = np.asarray(do, dtype=np.float64)
+    keys = np.concatenate([np.asarray(k, np.float64), np.asarray(kd, np.float64)])
+    vals = np.concatenate([np.asarray(v, np.float64), np.asarray(vd, np.float64)])
+    n = np.asarray(k).shape[0]
+    dq = np.empty_like(q)
+    dkd = np.zeros((keys.shape[0] - n, q.shape[1]))
+    dvd = np.zeros_like(dkd)
+    for g in range(q.shape[0]):
+        s = keys @ q[g] * scale
+        w = np.exp(s - s.max())
+        w /= w.sum()
+        o = w @ vals
+        ds = w * (vals @ do[g] - do[g] @ o)
+        dq[g] = scale * ds @ keys
+        dkd += scale * np.outer(ds[n:], q[g])
+        dvd += np.outer(w[n:], do[g])
+    return dict(dQ=dq, dK_depth=dkd, dV_depth=dvd)
+
+
 def moda_attention_grads(Q, K, V, K_depth, V_depth, num_layers, dO, scale=None,
                          dtype=np.float64):
     """Gradients of moda_attention_naive (moda_naive.py:13-162) for an upstream dO.

@@ -194,3 +194,32 @@ def test_depth_backward_tensor_core_range(case, dtype):
     torch.cuda.synchronize()
     for g, k in zip(grads, GRADS):
         assert half_ok(host(g), ref[k]), (k, float(np.max(np.abs(host(g) - ref[k]))))
+
+
+@pytest.mark.slow
+def test_kernel_only_config_backward_sampled_tokens():
+    # B=1 of the kernel-only configuration (H_q=32, H_k=8, T=8192, d=128, L=32), bf16:
+    # dQ rows and the depth rows' gradients of sampled tokens, exactly per token in fp64
+    B, Hq, Hk, T, d, L = 1, 32, 8, 8192, 128, 32
+    G = Hq // Hk
+    g = torch.Generator(device="cuda").manual_seed(9)
+    mk = lambda *s: torch.randn(*s, device="cuda", generator=g, dtype=torch.bfloat16)
+    Q, K, V, dO = mk(B, Hq, T, d), mk(B, Hk, T, d), mk(B, Hk, T, d), mk(B, Hq, T, d)
+    Kd, Vd = mk(B, Hk, T * L, d), mk(B, Hk, T * L, d)
+    O, lse = moda_forward_lse(Q, K, V, Kd, Vd, L)
+    dQ, dK, dV, dKd, dVd = moda_backward(dO, Q, K, V, Kd, Vd, O, lse, L)
+    torch.cuda.synchronize()
+    for t_ in (dQ, dK, dV, dKd, dVd):
+        assert torch.isfinite(t_).all()
+    h = lambda x: x.float().cpu().numpy()
+    rng = np.random.default_rng(3)
+    picks = [(0, 0), (Hk - 1, T - 1), (3, 4095), (5, 128)]
+    picks += [(int(rng.integers(Hk)), int(rng.integers(T))) for _ in range(8)]
+    for hk, t in picks:
+        heads = slice(hk * G, (hk + 1) * G)
+        rows = slice(t * L, (t + 1) * L)
+        ref = orc.moda_token_grads(h(Q[0, heads, t]), h(dO[0, heads, t]), h(K[0, hk, :t + 1]),
+                                   h(V[0, hk, :t + 1]), h(Kd[0, hk, rows]), h(Vd[0, hk, rows]), d ** -0.5)
+        assert half_ok(h(dQ[0, heads, t]), ref["dQ"]), ("dQ", hk, t)
+        assert half_ok(h(dKd[0, hk, rows]), ref["dK_depth"]), ("dK_depth", hk, t)
+        assert half_ok(h(dVd[0, hk, rows]), ref["dV_depth"]), ("dV_depth", hk, t)

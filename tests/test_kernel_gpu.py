@@ -224,3 +224,27 @@ def test_kernel_only_benchmark_config_sampled_rows():
                            Kd[b, hk, t * L:(t + 1) * L].cpu().double().numpy(),
                            Vd[b, hk, t * L:(t + 1) * L].cpu().double().numpy(), d ** -0.5)
         assert max_abs(out[b, h, t].float().cpu().numpy(), ref) <= BF16_ABS_TOL, (b, h, t)
+
+
+@pytest.mark.slow
+def test_scaling_config_one_batch_sampled_rows():
+    # one batch of the multi-GPU configuration (H_q=64, H_k=8: G=8, T=16384, d=128, L=48),
+    # bf16: the G=8 tiling, 48 depth rows per token and the longest sequences
+    B, Hq, Hk, T, d, L = 1, 64, 8, 16384, 128, 48
+    g = torch.Generator(device="cuda").manual_seed(4)
+    mk = lambda *s: torch.randn(*s, device="cuda", generator=g, dtype=torch.bfloat16)
+    Q, K, V = mk(B, Hq, T, d), mk(B, Hk, T, d), mk(B, Hk, T, d)
+    Kd, Vd = mk(B, Hk, T * L, d), mk(B, Hk, T * L, d)
+    out = moda_attention_cuda(Q, K, V, Kd, Vd, L, chunk_size=128)
+    assert torch.isfinite(out).all()
+    rng = np.random.default_rng(1)
+    rows = [(0, 0, 0), (0, Hq - 1, T - 1), (0, 9, 8191), (0, 40, 16)]
+    rows += [(0, int(rng.integers(Hq)), int(rng.integers(T))) for _ in range(12)]
+    G = Hq // Hk
+    for (b, h, t) in rows:
+        hk = h // G
+        ref = orc.moda_row(Q[b, h, t].cpu().double().numpy(), K[b, hk, :t + 1].cpu().double().numpy(),
+                           V[b, hk, :t + 1].cpu().double().numpy(),
+                           Kd[b, hk, t * L:(t + 1) * L].cpu().double().numpy(),
+                           Vd[b, hk, t * L:(t + 1) * L].cpu().double().numpy(), d ** -0.5)
+        assert max_abs(out[b, h, t].float().cpu().numpy(), ref) <= BF16_ABS_TOL, (b, h, t)

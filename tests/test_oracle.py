@@ -129,3 +129,22 @@ def test_grad_oracle_lse_matches_forward():
     q, k, kd = f64(z["Q"][0, 1, 5]), f64(z["K"][0, 0, :6]), f64(z["K_depth"][0, 0, 5 * meta["L"]:6 * meta["L"]])
     s = np.concatenate([k @ q, kd @ q]) * z["Q"].shape[-1] ** -0.5
     assert abs(r["lse"][0, 1, 5] - (s.max() + np.log(np.exp(s - s.max()).sum()))) < 1e-9
+
+
+def test_token_grads_match_reference_autograd_fixtures():
+    # the per-token restatement used for full-size spot checks, against the reference's
+    # own fp64 autograd (tests/golden/make_golden.py: grad_case)
+    for name in ("grad_b1_h4x2_t32_d64_l8", "grad_b1_h8x2_t20_d64_l3_extra8"):
+        z, meta = load_golden(name)
+        L = meta["L"]
+        G = z["Q"].shape[1] // z["K"].shape[1]
+        scale = meta.get("scale") or z["Q"].shape[-1] ** -0.5
+        for (b, hk, t) in [(0, 0, 0), (0, 1, 7), (0, 0, z["Q"].shape[2] - 1)]:
+            heads = slice(hk * G, (hk + 1) * G)
+            r = orc.moda_token_grads(z["Q"][b, heads, t], z["dO"][b, heads, t], z["K"][b, hk, :t + 1],
+                                     z["V"][b, hk, :t + 1], z["K_depth"][b, hk, t * L:(t + 1) * L],
+                                     z["V_depth"][b, hk, t * L:(t + 1) * L], scale)
+            # the fixtures store the fp64 gradients as float32 (rounding ~1e-8 here)
+            assert max_abs(r["dQ"], z["dQ"][b, heads, t]) < 1e-6
+            assert max_abs(r["dK_depth"], z["dK_depth"][b, hk, t * L:(t + 1) * L]) < 1e-6
+            assert max_abs(r["dV_depth"], z["dV_depth"][b, hk, t * L:(t + 1) * L]) < 1e-6
