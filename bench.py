@@ -29,6 +29,12 @@ with the reference's cache lifecycle and again with the opt-in lean one.
 cache slot 5 of a [8, 4, 4096*48, 128] cache) against the same work as two library
 GEMMs plus the append kernel; ``--batch`` shrinks B for profiling.
 
+``--pass module`` (one GPU) times the standalone MoDAAttention forward of the module
+configuration (d_model 512, 8 query / 4 KV heads of 64, B=8, T=2048, 5 layers of depth
+rows in N(0,1) caches, bf16, random-init weights from seed 1): the whole module call
+(projections, fused kernel, output projection) and the fused kernel alone on its
+inputs, against the kernel's roofline.
+
 ``--pass triton-reference`` (one GPU) times the reference's own GPU path,
 ``moda_attention_triton`` (SDPA over repeat_interleave'd K/V plus its Triton depth
 combine kernel), installed unmodified in ``baseline/_ref`` and imported from there under
@@ -230,7 +236,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--pass", dest="which",
-                    choices=["forward", "backward", "model", "proj", "triton-reference"],
+                    choices=["forward", "backward", "model", "proj", "triton-reference", "module"],
                     default="forward")
     ap.add_argument("--batch", type=int, default=None, help="batch override for --pass proj")
     ap.add_argument("--kernel-shares", action="store_true",
@@ -247,6 +253,8 @@ def main():
         return run_proj(args)
     if args.which == "triton-reference":
         return run_triton_reference(args, wl)
+    if args.which == "module":
+        return run_module(args)
     args.warmup = max(args.warmup, 3)
 
     import torch
@@ -521,6 +529,69 @@ def run_model(args):
         "clocks": clk,
         "verify": {"finite": bool(torch.isfinite(outs[False]).all()),
                    "device_status": device_status(dev)},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_module(args):
+    """MoDAAttention standalone forward (module configuration) on one GPU."""
+    import torch
+    from moda import MoDAAttention, MoDAConfig
+    from moda.kernels import device_status
+    from moda.kernels.moda_cuda import moda_forward_into
+    args.warmup = max(args.warmup, 3)
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B, T, D, Hq, Hk, d, L = 8, 2048, 512, 8, 4, 64, 5
+    torch.manual_seed(1)
+    with torch.device(dev):
+        attn = MoDAAttention(MoDAConfig(d_model=D, num_heads=Hq, num_kv_heads=Hk, head_dim=d,
+                                        num_layers=L, chunk_size=64)).to(torch.bfloat16).eval()
+    g = torch.Generator(device=dev).manual_seed(1)
+    x = torch.randn(B, T, D, device=dev, generator=g).to(torch.bfloat16)
+    Kd = torch.randn(B, Hk, T * L, d, device=dev, generator=g).to(torch.bfloat16)
+    Vd = torch.randn(B, Hk, T * L, d, device=dev, generator=g).to(torch.bfloat16)
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn, steps):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(0) as clocks:
+            e0.record(stream)
+            for _ in range(steps):
+                fn()
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / steps, clocks.summary()
+
+    with torch.no_grad():
+        ms_mod, clk = timed(lambda: attn(x, Kd, Vd), args.steps)
+        # the kernel alone, on the module's own projected (strided) Q, K, V views
+        Q = attn.q_proj(x).view(B, T, Hq, d).transpose(1, 2)
+        K = attn.k_proj(x).view(B, T, Hk, d).transpose(1, 2)
+        V = attn.v_proj(x).view(B, T, Hk, d).transpose(1, 2)
+        O = torch.empty(B, Hq, T, d, device=dev, dtype=torch.bfloat16)
+        ms_k, _ = timed(lambda: moda_forward_into(O, Q, K, V, Kd, Vd, L, None, 64), 10 * args.steps)
+    fl = flops(B, Hq, T, d, L)
+    by = hbm_bytes(B, Hq, Hk, T, d, L)
+    p_tflops, p_gbs, p_kind = peaks()
+    t_roof = max(fl / (p_tflops * 1e12), by / (p_gbs * 1e9)) * 1e3
+    tflops = fl / (ms_k * 1e-3) / 1e12
+    line = {
+        "metric": "MoDAAttention module forward throughput (tokens/s)",
+        "value": B * T / (ms_mod * 1e-3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_mod, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic x, K_depth, V_depth ~ N(0,1) (seed 1), random-init weights (seed 1)",
+        "config": {"workload": "MoDAAttention standalone forward: d_model=512 H_q=8 H_k=4 d=64 "
+                               "B=8 T=2048, 5 layers of depth rows (num_layers=5)"},
+        "kernel": {"ms": ms_k, "tflops": tflops, "hbm_gbs": by / (ms_k * 1e-3) / 1e9,
+                   "roofline_ms": t_roof, "roofline_frac": t_roof / ms_k, "peak_kind": p_kind,
+                   "algorithmic_flops": fl, "algorithmic_bytes": by},
+        "clocks": clk,
+        "verify": {"finite": bool(torch.isfinite(O).all()), "device_status": device_status(dev)},
     }
     print(json.dumps(line), flush=True)
 
