@@ -239,6 +239,8 @@ def main():
                     choices=["forward", "backward", "model", "proj", "triton-reference", "module"],
                     default="forward")
     ap.add_argument("--batch", type=int, default=None, help="batch override for --pass proj")
+    ap.add_argument("--graph", action="store_true",
+                    help="--pass module / model: capture one forward as a CUDA graph and time replays")
     ap.add_argument("--kernel-shares", action="store_true",
                     help="--pass model: also print each path's per-kernel CUDA time (stderr)")
     args = ap.parse_args()
@@ -486,16 +488,18 @@ def run_model(args):
     for lean in (False, True):
         model.config.lean_depth_cache = lean
         with torch.no_grad():
+            step = graphed(lambda: model(x)) if args.graph else (lambda: model(x))
             for _ in range(args.warmup):
-                model(x)
+                step()
             torch.cuda.synchronize(dev)
             ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             with ClockSampler(0) as clocks:
                 ev0.record(stream)
                 for _ in range(args.steps):
-                    out = model(x)
+                    step()
                 ev1.record(stream)
                 torch.cuda.synchronize(dev)
+            out = model(x)
         ms = ev0.elapsed_time(ev1) / args.steps
         results[lean] = (ms, clocks.summary())
         outs[lean] = out.float()
@@ -522,7 +526,8 @@ def run_model(args):
         "dtype": "bf16", "data": "synthetic x ~ N(0,1) (seed 3), random-init weights (seed 3)",
         "config": {"workload": "full MoDAModel forward with DepthKVCache, post-norm, FFN depth "
                                "writes: d_model=2048 H_q=16 H_k=4 d=128 24 layers FFN 8192 "
-                               "B=8 T=4096", "global_batch": MODEL_B, "seq_len": MODEL_T},
+                               "B=8 T=4096", "global_batch": MODEL_B, "seq_len": MODEL_T,
+                   "launch": "CUDA graph replay" if args.graph else "eager"},
         "lean": {"value": tokens / (ms_lean * 1e-3), "unit": "tokens/s", "ms_per_step": ms_lean,
                  "max_abs_diff_vs_default": float(diff.max()),
                  "mean_abs_diff_vs_default": float(diff.mean()), "clocks": clk_lean},
@@ -531,6 +536,22 @@ def run_model(args):
                    "device_status": device_status(dev)},
     }
     print(json.dumps(line), flush=True)
+
+
+def graphed(fn, warmup=2):
+    """Capture fn() once as a CUDA graph (after warm-up calls on a side stream, which
+    also run the library's one-time setup) and return a replay callable."""
+    import torch
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(warmup):
+            fn()
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    return g.replay
 
 
 def run_module(args):
@@ -567,7 +588,8 @@ def run_module(args):
         return e0.elapsed_time(e1) / steps, clocks.summary()
 
     with torch.no_grad():
-        ms_mod, clk = timed(lambda: attn(x, Kd, Vd), args.steps)
+        fwd = (lambda: attn(x, Kd, Vd))
+        ms_mod, clk = timed(graphed(fwd) if args.graph else fwd, args.steps)
         # the kernel alone, on the module's own projected (strided) Q, K, V views
         Q = attn.q_proj(x).view(B, T, Hq, d).transpose(1, 2)
         K = attn.k_proj(x).view(B, T, Hk, d).transpose(1, 2)
@@ -586,7 +608,8 @@ def run_module(args):
         "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic x, K_depth, V_depth ~ N(0,1) (seed 1), random-init weights (seed 1)",
         "config": {"workload": "MoDAAttention standalone forward: d_model=512 H_q=8 H_k=4 d=64 "
-                               "B=8 T=2048, 5 layers of depth rows (num_layers=5)"},
+                               "B=8 T=2048, 5 layers of depth rows (num_layers=5)",
+                   "launch": "CUDA graph replay" if args.graph else "eager"},
         "kernel": {"ms": ms_k, "tflops": tflops, "hbm_gbs": by / (ms_k * 1e-3) / 1e9,
                    "roofline_ms": t_roof, "roofline_frac": t_roof / ms_k, "peak_kind": p_kind,
                    "algorithmic_flops": fl, "algorithmic_bytes": by},

@@ -219,3 +219,39 @@ def test_output_written_in_projection_layout_equals_contiguous(dtype):
         fast = attn(x, kd, kd)[0]
     slow = attn(x, kd, kd)[0].detach()  # grad enabled: the copying path
     assert torch.equal(fast, slow)
+
+
+def test_cuda_graph_replay_matches_eager():
+    # The library launches on the caller's stream and does all host work (tensor maps,
+    # attribute opt-ins) before its launches, so a forward can be captured once and
+    # replayed: MoDAAttention and the whole MoDAModel (cache zero-fill, attention,
+    # fused depth writes) replay bit-exactly.
+    torch.manual_seed(0)
+    cfg = MoDAConfig(d_model=256, num_heads=4, num_kv_heads=2, head_dim=64, num_layers=3,
+                     max_seq_len=128)
+    attn = MoDAAttention(cfg).cuda().to(torch.bfloat16).eval()
+    model = MoDAModel(cfg).cuda().to(torch.bfloat16).eval()
+    x = torch.randn(2, 128, 256, device="cuda", dtype=torch.bfloat16)
+    kd = torch.randn(2, 2, 128 * 3, 64, device="cuda", dtype=torch.bfloat16)
+    vd = torch.randn_like(kd)
+    with torch.no_grad():
+        eager_a = attn(x, kd, vd)[0].clone()
+        eager_m = model(x).clone()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):  # warm-up on a side stream, as capture requires
+            for _ in range(2):
+                attn(x, kd, vd)
+                model(x)
+        torch.cuda.current_stream().wait_stream(s)
+        ga, gm = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        with torch.cuda.graph(ga):
+            out_a = attn(x, kd, vd)[0]
+        with torch.cuda.graph(gm):
+            out_m = model(x)
+        for _ in range(3):
+            ga.replay()
+            gm.replay()
+        torch.cuda.synchronize()
+    assert torch.equal(out_a, eager_a)
+    assert torch.equal(out_m, eager_m)
