@@ -1,0 +1,57 @@
+"""The one-JSON-line contract of bench.py, checked on its CPU-only reference arm.
+
+The reference arm times the numpy restatement of moda_attention_naive on the host
+cores, so it runs here without a GPU; its line carries the same keys the GPU arm
+prints. Under torchrun with two ranks only rank 0 prints and the other rank exits 0
+without work.
+"""
+
+import json
+import os
+import subprocess
+import sys
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+BASE_KEYS = {"metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step",
+             "higher_is_better", "scaling", "vs_baseline", "dtype", "data", "config"}
+
+
+def _json_lines(out):
+    return [json.loads(s) for s in out.splitlines() if s.startswith("{")]
+
+
+def _check_reference_line(line, n_gpus):
+    assert BASE_KEYS <= set(line)
+    assert line["impl"] == "reference"
+    assert line["n_gpus"] == n_gpus and line["steps"] == 1 and line["warmup"] == 0
+    assert line["value"] > 0 and line["ms_per_step"] > 0 and line["higher_is_better"] is True
+    assert "workload" in line["config"]
+    cb = line["cpu_baseline"]
+    assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["value"] == line["value"]
+    assert cb["unit"] == line["unit"] and cb["sample"]
+    e2e = line["e2e"]
+    assert e2e["value"] == line["value"] and e2e["unit"] == line["unit"]
+    assert e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
+
+
+def test_reference_arm_prints_one_contract_line():
+    r = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--steps", "1",
+                        "--warmup", "0"], cwd=REPO, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = _json_lines(r.stdout)
+    assert len(lines) == 1
+    _check_reference_line(lines[0], 1)
+
+
+def test_reference_arm_two_ranks_rank0_only():
+    env = dict(os.environ, MASTER_ADDR="127.0.0.1")
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+                        "--nproc-per-node", "2", "--master-addr", "127.0.0.1",
+                        "--master-port", "29611", "bench.py", "--impl", "reference",
+                        "--gpus", "2", "--steps", "1", "--warmup", "0"],
+                       cwd=REPO, capture_output=True, text=True, timeout=300, env=env)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = _json_lines(r.stdout)
+    assert len(lines) == 1
+    _check_reference_line(lines[0], 2)
