@@ -78,31 +78,6 @@ MODA_DEV float fmax3(float a, float b, float c) {
     return d;
 }
 
-// Base-2 exponential of a pair on the FMA pipe (no MUFU), for inputs <= 126:
-// Cody-Waite reduction x = n + f (n = round(x) via the 1.5*2^23 trick, f in
-// [-1/2, 1/2]), 2^f by a degree-3 relative-minimax polynomial (Remez), 2^n by
-// adding n to the exponent field. Inputs below -125 (including -inf) are clamped
-// to -125, i.e. map to ~2e-38 instead of 0. Relative error <= 7.5e-5; the
-// coefficients come from csrc/gen_exp2_poly.py.
-MODA_DEV void exp2_poly_pair(uint64_t x2, float& r0, float& r1) {
-    float x0, x1;
-    f2_unpack(x2, x0, x1);
-    x2 = f2_pack(fmaxf(x0, -125.f), fmaxf(x1, -125.f));
-    const uint64_t magic = f2_pack(12582912.f, 12582912.f);
-    const uint64_t t = f2_add(x2, magic);
-    const uint64_t n = f2_add(t, f2_pack(-12582912.f, -12582912.f));
-    const uint64_t f = f2_fma(n, f2_pack(-1.f, -1.f), x2);
-    uint64_t p = f2_fma(f2_pack(5.517166853e-02f, 5.517166853e-02f), f,
-                        f2_pack(2.426111251e-01f, 2.426111251e-01f));
-    p = f2_fma(p, f, f2_pack(6.932609677e-01f, 6.932609677e-01f));
-    p = f2_fma(p, f, f2_pack(9.999280572e-01f, 9.999280572e-01f));
-    float p0, p1, t0, t1;
-    f2_unpack(p, p0, p1);
-    f2_unpack(t, t0, t1);
-    r0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
-    r1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
-}
-
 // ------------------------------------------------------------------ mbarrier
 MODA_DEV void mbar_init(uint32_t bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
@@ -195,21 +170,6 @@ MODA_DEV void tma_load_4d(const CUtensorMap* m, uint32_t dst, uint32_t bar, int 
         " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
         "l"(reinterpret_cast<uint64_t>(m)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
         : "memory");
-}
-
-MODA_DEV void tma_store_4d(const CUtensorMap* m, uint32_t src, int c0, int c1, int c2, int c3) {
-    asm volatile(
-        "cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
-            reinterpret_cast<uint64_t>(m)),
-        "r"(src), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
-        : "memory");
-}
-
-MODA_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-MODA_DEV void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
-MODA_DEV void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
-MODA_DEV void fence_proxy_async_smem() {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 MODA_DEV void named_bar_sync(int id, int nthreads) {
@@ -312,17 +272,6 @@ MODA_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
         : "memory");
 }
 
-MODA_DEV void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
-        "%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-          "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr)
-        : "memory");
-}
-
 MODA_DEV void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
@@ -334,21 +283,11 @@ MODA_DEV void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
 }
 
 // ------------------------------------------------------------------ UMMA descriptors
-// Shared-memory matrix descriptor (sm_100 format, version 1), 128-byte swizzle.
+// Shared-memory matrix descriptor (sm_100 format, version 1), 128-byte swizzle:
 //   bits  0-13 start address >> 4     bits 16-29 leading byte offset >> 4
 //   bits 32-45 stride byte offset >> 4 bits 46-47 version (1)
 //   bits 61-63 layout (2 = 128B swizzle)
-MODA_DEV uint64_t smem_desc_sw128(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
-    uint64_t d = 0;
-    d |= static_cast<uint64_t>((addr >> 4) & 0x3FFFu);
-    d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
-    d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
-    d |= static_cast<uint64_t>(1) << 46;
-    d |= static_cast<uint64_t>(2) << 61;
-    return d;
-}
-
-// The same descriptor split in two 32-bit words, so the issue loop advances the
+// Built as two 32-bit words, so the issue loop advances the
 // start address with one 32-bit add: lo = (addr >> 4) | (lbo >> 4) << 16,
 // hi = (sbo >> 4) | version << 14 | layout << 29. Valid while addr < 256 KB.
 __host__ __device__ constexpr uint32_t desc_hi_sw128(uint32_t sbo_bytes) {
