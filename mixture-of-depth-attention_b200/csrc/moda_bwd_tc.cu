@@ -1049,13 +1049,14 @@ static bool launch_depth_mma_hd(const BwdParams& p, cudaStream_t stream) {
     const long long want = (n + kDmWarps - 1) / kDmWarps;
     const int grid = static_cast<int>(want < 2LL * sm_count() ? want : 2LL * sm_count());
     const int smem = kDmWarps * C::kWarp;
-    auto launch = [&](auto kern) {
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-            return false;
+    static std::atomic<uint64_t> done_bf16{0}, done_f16{0};
+    auto launch = [&](auto kern, std::atomic<uint64_t>& done) {
+        if (ensure_smem_attr(done, kern, smem) != cudaSuccess) return false;
         kern<<<grid, kDmWarps * 32, smem, stream>>>(p);
         return true;
     };
-    return p.dtype == MODA_BF16 ? launch(moda_bwd_depth_mma_kernel<HD, 1>) : launch(moda_bwd_depth_mma_kernel<HD, 0>);
+    return p.dtype == MODA_BF16 ? launch(moda_bwd_depth_mma_kernel<HD, 1>, done_bf16)
+                                : launch(moda_bwd_depth_mma_kernel<HD, 0>, done_f16);
 }
 
 // The tensor-core depth kernel for 16-bit inputs with d in {64, 128}, whole tokens per
@@ -1159,12 +1160,8 @@ template <int HD, int FMT, int MODE>
 static int launch_bwd_inst(const TcBwdParams& tp, int items, cudaStream_t stream) {
     using Cfg = BwdCfg<HD>;
     auto kern = moda_bwd_tc_kernel<HD, FMT, MODE>;
-    static bool attr_set = false;
-    if (!attr_set) {
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem) != cudaSuccess)
-            return MODA_ERR_LAUNCH;
-        attr_set = true;
-    }
+    static std::atomic<uint64_t> attr_done{0};
+    if (ensure_smem_attr(attr_done, kern, Cfg::kSmem) != cudaSuccess) return MODA_ERR_LAUNCH;
     if (items == 0) return MODA_OK;
     const int grid = items < sm_count() ? items : sm_count();
     kern<<<grid, kBThreads, Cfg::kSmem, stream>>>(tp);

@@ -799,18 +799,19 @@ template <int HD, int FMT>
 static int launch_tc_inst(const TcParams& tp, int grid, cudaStream_t stream) {
     using Cfg = TcCfg<HD>;
     auto kern = moda_fwd_tc_kernel<HD, FMT>;
-    static bool attr_set = false;
-    if (!attr_set) {
-        // The setmaxnreg split assumes exactly kLaunchRegs registers per thread at
-        // launch; with fewer, the softmax warpgroups' increase could never be granted.
+    static std::atomic<uint64_t> attr_done{0};
+    static std::atomic<int> num_regs{0};  // registers per thread of the compiled kernel, once known
+    int nr = num_regs.load(std::memory_order_relaxed);
+    if (nr == 0) {
         cudaFuncAttributes fa;
-        if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess || fa.numRegs != kLaunchRegs)
-            return MODA_ERR_UNSUPPORTED;
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 Cfg::kSmemBytes) != cudaSuccess)
-            return MODA_ERR_LAUNCH;
-        attr_set = true;
+        if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) return MODA_ERR_UNSUPPORTED;
+        nr = fa.numRegs;
+        num_regs.store(nr, std::memory_order_relaxed);
     }
+    // The setmaxnreg split assumes exactly kLaunchRegs registers per thread at
+    // launch; with fewer, the softmax warpgroups' increase could never be granted.
+    if (nr != kLaunchRegs) return MODA_ERR_UNSUPPORTED;
+    if (ensure_smem_attr(attr_done, kern, Cfg::kSmemBytes) != cudaSuccess) return MODA_ERR_LAUNCH;
     kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(tp);
     return MODA_OK;
 }

@@ -4,6 +4,9 @@
 #include "../../include/moda_b200.h"
 #include "moda_common.cuh"
 
+#include <atomic>
+#include <cstdint>
+
 namespace moda {
 
 // Validated forward problem. Strides are in elements.
@@ -110,5 +113,20 @@ constexpr int kMaxDevices = 64;
 // Device address of the library's fixed backward scratch on the current device.
 cudaError_t noalloc_scratch(void** ptr);
 cudaError_t read_and_clear_status(cudaStream_t stream, int* value);
+
+// One-time opt-in of a kernel's dynamic shared memory on the current device (function
+// attributes are per device). `done` is the kernel's own bitmask of devices already set
+// up; devices past 63 are set up on every call.
+template <typename Kernel>
+cudaError_t ensure_smem_attr(std::atomic<uint64_t>& done, Kernel kern, int bytes) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const uint64_t bit = dev >= 0 && dev < 64 ? (1ull << dev) : 0ull;
+    if (bit != 0 && (done.load(std::memory_order_acquire) & bit) != 0) return cudaSuccess;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess && bit != 0) done.fetch_or(bit, std::memory_order_release);
+    return e;
+}
 
 }  // namespace moda

@@ -218,16 +218,12 @@ __global__ void __launch_bounds__(kPThreads, 1)
     }
 }
 
-// One shared-memory opt-in per instantiation (each has its own flag).
+// One shared-memory opt-in per instantiation and device (each instantiation has its own mask).
 template <int FMT>
 int launch_proj_inst(const ProjParams& p, int grid, cudaStream_t stream) {
-    static bool attr_set = false;
-    if (!attr_set) {
-        if (cudaFuncSetAttribute(moda_proj_append_kernel<FMT>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmemBytes) != cudaSuccess)
-            return MODA_ERR_LAUNCH;
-        attr_set = true;
-    }
+    static std::atomic<uint64_t> attr_done{0};
+    if (ensure_smem_attr(attr_done, moda_proj_append_kernel<FMT>, kPSmemBytes) != cudaSuccess)
+        return MODA_ERR_LAUNCH;
     moda_proj_append_kernel<FMT><<<grid, kPThreads, kPSmemBytes, stream>>>(p);
     return MODA_OK;
 }

@@ -296,6 +296,8 @@ def depth_proj_append(x: Tensor, w_kv: Tensor, k_cache: Tensor, v_cache: Tensor,
     for n, t in (("x", x), ("w_kv", w_kv), ("k_cache", k_cache), ("v_cache", v_cache)):
         if t.device.type != "cuda":
             raise RuntimeError(f"depth projection runs on CUDA tensors only ({n} is on {t.device})")
+        if t.device != x.device:
+            raise RuntimeError(f"{n} is on {t.device}, x on {x.device}")
         if t.dtype != x.dtype:
             raise TypeError(f"{n} has dtype {t.dtype}, x has {x.dtype}")
     if x.dim() != 3 or w_kv.dim() != 2:
@@ -351,8 +353,11 @@ def depth_append_autograd(k_cache: Tensor, v_cache: Tensor, layer_idx: int, k: T
 
 
 def device_status(device=None) -> int:
-    """Read and clear the kernels' timeout status word (0 = no bounded wait expired)."""
+    """Read and clear the kernels' timeout status word of ``device`` (default: the current
+    device); 0 = no bounded wait expired."""
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
     stream = torch.cuda.current_stream(device).cuda_stream
-    code = _lib.load().moda_device_status(stream)
+    with torch.cuda.device(device):
+        code = _lib.load().moda_device_status(stream)
     _lib.check(code, "moda_device_status")
     return code
