@@ -535,9 +535,13 @@ __global__ void __launch_bounds__(kThreads, 1) moda_fwd_tc_kernel(const __grid_c
                 lo -= 64 * half;  // into this warp's column range
                 hi -= 64 * half;
                 const bool live = !need_mask || (lo < hi && hi > 0 && lo < 64);
+                // With L a multiple of 32 a depth block's window [lo, hi) covers whole
+                // 32-column chunks: pick chunks per row instead of masking each score.
+                const bool chunked = st.dep && (p.L & 31) == 0;
+                const bool ok0 = lo <= 0 && hi >= 32, ok1 = lo <= 32 && hi >= 64;
                 float mx = -INFINITY;
                 if (__any_sync(0xffffffffu, live)) {
-                    if (need_mask) {
+                    if (need_mask && !chunked) {
 #pragma unroll
                         for (int c = 0; c < 64; ++c) {
                             const bool keep = (c >= lo) && (c < hi);
@@ -553,7 +557,10 @@ __global__ void __launch_bounds__(kThreads, 1) moda_fwd_tc_kernel(const __grid_c
                             a = fmax3(a, __uint_as_float(sv[16 * k + i]), __uint_as_float(sv[16 * k + i + 1]));
                         mx4[k] = fmaxf(a, __uint_as_float(sv[16 * k + 15]));
                     }
-                    mx = fmaxf(fmax3(mx4[0], mx4[1], mx4[2]), mx4[3]);
+                    if (chunked)
+                        mx = fmaxf(ok0 ? fmaxf(mx4[0], mx4[1]) : -INFINITY, ok1 ? fmaxf(mx4[2], mx4[3]) : -INFINITY);
+                    else
+                        mx = fmaxf(fmax3(mx4[0], mx4[1], mx4[2]), mx4[3]);
                 }
                 // trade partial row maxima with the partner warp (double-buffered by block parity)
                 float* xm = xmax + (nblk & 1u) * 256;
@@ -578,13 +585,15 @@ __global__ void __launch_bounds__(kThreads, 1) moda_fwd_tc_kernel(const __grid_c
                 if (__any_sync(0xffffffffu, live)) {
                     const float m_base = (m_use == -INFINITY) ? 0.f : m_use;
                     const uint64_t sc2 = f2_pack(sc, sc);
-                    const uint64_t nm2 = f2_pack(-m_base, -m_base);
                     uint64_t acc[4];
 #pragma unroll
                     for (int k = 0; k < 4; ++k) acc[k] = 0ull;
 #pragma unroll
                     for (int q4 = 0; q4 < 2; ++q4) {
                         uint32_t pk[16];
+                        // a chunk outside the row's depth window gives exp2(-inf) = 0
+                        const float nbq = (chunked && !(q4 == 0 ? ok0 : ok1)) ? -INFINITY : -m_base;
+                        const uint64_t nm2 = f2_pack(nbq, nbq);
 #pragma unroll
                         for (int c = 0; c < 32; c += 2) {
                             const int cc = 32 * q4 + c;

@@ -82,6 +82,12 @@ SHAPES = [
     (1, 64, 8, 70, 128, 48),
     (1, 8, 8, 90, 64, 12),
     (1, 128, 1, 40, 64, 3),
+    # L a multiple of 32: depth windows are whole 32-column chunks
+    (1, 16, 2, 150, 64, 64),
+    (1, 2, 2, 70, 128, 32),
+    (1, 4, 2, 45, 64, 96),
+    (1, 32, 2, 50, 128, 32),
+    (1, 32, 1, 20, 64, 32),
 ]
 
 
