@@ -535,17 +535,25 @@ __global__ void __launch_bounds__(kThreads, 1) moda_fwd_tc_kernel(const __grid_c
                 lo -= 64 * half;  // into this warp's column range
                 hi -= 64 * half;
                 const bool live = !need_mask || (lo < hi && hi > 0 && lo < 64);
-                // With L a multiple of 32 a depth block's window [lo, hi) covers whole
-                // 32-column chunks: pick chunks per row instead of masking each score.
-                const bool chunked = st.dep && (p.L & 31) == 0;
-                const bool ok0 = lo <= 0 && hi >= 32, ok1 = lo <= 32 && hi >= 64;
+                // With L a multiple of 16 a depth block's window [lo, hi) covers whole
+                // 16-column groups: pick groups per row instead of masking each score.
+                const bool chunked = st.dep && (p.L & 15) == 0;
+                bool ok[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) ok[k] = lo <= 16 * k && hi >= 16 * k + 16;
                 float mx = -INFINITY;
                 if (__any_sync(0xffffffffu, live)) {
                     if (need_mask && !chunked) {
+                        if (st.dep) {
 #pragma unroll
-                        for (int c = 0; c < 64; ++c) {
-                            const bool keep = (c >= lo) && (c < hi);
-                            sv[c] = keep ? sv[c] : __float_as_uint(-INFINITY);
+                            for (int c = 0; c < 64; ++c) {
+                                const bool keep = (c >= lo) && (c < hi);
+                                sv[c] = keep ? sv[c] : __float_as_uint(-INFINITY);
+                            }
+                        } else {  // causal diagonal: lo <= 0, only the upper bound bites
+#pragma unroll
+                            for (int c = 0; c < 64; ++c)
+                                sv[c] = c < hi ? sv[c] : __float_as_uint(-INFINITY);
                         }
                     }
                     float mx4[4];
@@ -558,7 +566,8 @@ __global__ void __launch_bounds__(kThreads, 1) moda_fwd_tc_kernel(const __grid_c
                         mx4[k] = fmaxf(a, __uint_as_float(sv[16 * k + 15]));
                     }
                     if (chunked)
-                        mx = fmaxf(ok0 ? fmaxf(mx4[0], mx4[1]) : -INFINITY, ok1 ? fmaxf(mx4[2], mx4[3]) : -INFINITY);
+                        mx = fmaxf(fmaxf(ok[0] ? mx4[0] : -INFINITY, ok[1] ? mx4[1] : -INFINITY),
+                                   fmaxf(ok[2] ? mx4[2] : -INFINITY, ok[3] ? mx4[3] : -INFINITY));
                     else
                         mx = fmaxf(fmax3(mx4[0], mx4[1], mx4[2]), mx4[3]);
                 }
@@ -591,14 +600,16 @@ __global__ void __launch_bounds__(kThreads, 1) moda_fwd_tc_kernel(const __grid_c
 #pragma unroll
                     for (int q4 = 0; q4 < 2; ++q4) {
                         uint32_t pk[16];
-                        // a chunk outside the row's depth window gives exp2(-inf) = 0
-                        const float nbq = (chunked && !(q4 == 0 ? ok0 : ok1)) ? -INFINITY : -m_base;
-                        const uint64_t nm2 = f2_pack(nbq, nbq);
+                        // a group outside the row's depth window gives exp2(-inf) = 0
+                        const float nba = (chunked && !ok[2 * q4]) ? -INFINITY : -m_base;
+                        const float nbb = (chunked && !ok[2 * q4 + 1]) ? -INFINITY : -m_base;
+                        const uint64_t nma = f2_pack(nba, nba), nmb = f2_pack(nbb, nbb);
 #pragma unroll
                         for (int c = 0; c < 32; c += 2) {
                             const int cc = 32 * q4 + c;
                             const uint64_t xx = f2_fma(
-                                f2_pack(__uint_as_float(sv[cc]), __uint_as_float(sv[cc + 1])), sc2, nm2);
+                                f2_pack(__uint_as_float(sv[cc]), __uint_as_float(sv[cc + 1])), sc2,
+                                c < 16 ? nma : nmb);
                             float x0, x1;
                             f2_unpack(xx, x0, x1);
                             const float p0 = ex2(x0), p1 = ex2(x1);

@@ -82,7 +82,9 @@ SHAPES = [
     (1, 64, 8, 70, 128, 48),
     (1, 8, 8, 90, 64, 12),
     (1, 128, 1, 40, 64, 3),
-    # L a multiple of 32: depth windows are whole 32-column chunks
+    # L a multiple of 16 (or 32): depth windows are whole 16-column groups
+    (1, 8, 2, 90, 128, 16),
+    (2, 16, 2, 77, 64, 48),
     (1, 16, 2, 150, 64, 64),
     (1, 2, 2, 70, 128, 32),
     (1, 4, 2, 45, 64, 96),
