@@ -583,11 +583,10 @@ __global__ void __launch_bounds__(kThreads, 1) moda_fwd_tc_kernel(const __grid_c
                 const float alpha = rescale ? ex2(m_run - m_use) : 1.0f;
                 m_run = m_use;
                 // wait for the other tile's turn to end (bounded; skipped after an abort)
+                // (a hint only: at most 2^20 polls, and no clock read on this hot path)
                 if (lane == 0) {
                     const uint32_t need = 8u * turn_target;
-                    const long long t0 = clock64();
-                    while (*other_turns < need && !*abort_flag) {
-                        if (clock64() - t0 > kWaitLimitCycles / 64) break;  // hint only: never stall long
+                    for (uint32_t it = 0; it < (1u << 20) && *other_turns < need && !*abort_flag; ++it) {
                     }
                 }
                 __syncwarp();
