@@ -121,8 +121,12 @@ int moda_bwd(const ModaTensor* q, const ModaTensor* k, const ModaTensor* v, cons
  * array compiled into the library (MODA_NOALLOC_ROWS floats per device, its address
  * resolved once per device), so the call allocates nothing and needs no buffer from
  * the caller. B*H_q*T > MODA_NOALLOC_ROWS is rejected with MODA_ERR_UNSUPPORTED
- * before anything else. The array is shared by all calls on a device: such calls
- * must not overlap in time (issue them on one stream, or synchronize).
+ * before anything else (each of B, H_q and T is bounded before they are multiplied).
+ * The array is shared by all calls on a device: such calls must not overlap in time
+ * (issue them on one stream, or synchronize). The address is resolved on the first
+ * call on each device and kept for the life of the process; cudaDeviceReset (or any
+ * other teardown of the device's primary context) between calls is not supported,
+ * since the kept address would then be stale.
  * No reference counterpart (the reference's autograd allocates through torch). */
 int moda_bwd_noalloc(const ModaTensor* q, const ModaTensor* k, const ModaTensor* v,
                      const ModaTensor* kd, const ModaTensor* vd, const ModaTensor* o,

@@ -212,11 +212,25 @@ int moda_bwd_noalloc(const ModaTensor* q, const ModaTensor* k, const ModaTensor*
     g_err[0] = 0;
     // Size check first, before anything else touches the descriptors or CUDA.
     if (!q) return fail(MODA_ERR_ARG, "null tensor descriptor");
-    const int64_t rows = q->sizes[0] * q->sizes[1] * q->sizes[2];
-    if (q->sizes[0] < 0 || q->sizes[1] < 0 || q->sizes[2] < 0 || rows > MODA_NOALLOC_ROWS)
+    // Each factor is checked before it is multiplied, so no product can overflow or
+    // wrap back under the limit.
+    int64_t rows = 1;
+    for (int i = 0; i < 3; ++i) {
+        if (q->sizes[i] < 0)
+            return fail(MODA_ERR_SHAPE, "negative size %lld in dimension %d of q",
+                        (long long)q->sizes[i], i);
+        if (q->sizes[i] > MODA_NOALLOC_ROWS || __builtin_mul_overflow(rows, q->sizes[i], &rows) ||
+            rows > MODA_NOALLOC_ROWS) {
+            rows = -1;
+            break;
+        }
+    }
+    if (rows < 0 && q->sizes[0] != 0 && q->sizes[1] != 0 && q->sizes[2] != 0)
         return fail(MODA_ERR_UNSUPPORTED,
-                    "moda_bwd_noalloc handles up to %d query rows (B*H_q*T), got %lld",
-                    MODA_NOALLOC_ROWS, (long long)rows);
+                    "moda_bwd_noalloc handles up to %d query rows (B*H_q*T), got %lld x %lld x %lld",
+                    MODA_NOALLOC_ROWS, (long long)q->sizes[0], (long long)q->sizes[1],
+                    (long long)q->sizes[2]);
+    if (rows < 0) rows = 0;  // an empty dimension (with an oversize one): no rows
     void* scratch = nullptr;
     if (rows > 0 && moda::noalloc_scratch(&scratch) != cudaSuccess)
         return fail(MODA_ERR_LAUNCH, "could not resolve the library's backward scratch");

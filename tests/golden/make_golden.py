@@ -1,8 +1,9 @@
 """Generate the golden fixtures in this folder by running the reference itself.
 
-Run (in a container that has the reference checkout):
+Run (in a container that has the reference checkout), giving the checkout's path
+either as an argument or in the MODA_REFERENCE environment variable:
 
-    python tests/golden/make_golden.py --reference /root/reference
+    python tests/golden/make_golden.py --reference <path to the reference checkout>
 
 It imports ``moda`` from the reference checkout (pure Python/PyTorch, CPU,
 fp32) and records seeded inputs and the reference's outputs as ``.npz`` files.
@@ -158,8 +159,11 @@ def cache_case():
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("MODA_REFERENCE"),
+                    help="path of the reference checkout (default: $MODA_REFERENCE)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference PATH or set MODA_REFERENCE")
     sys.path.insert(0, args.reference)
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     cases = [
