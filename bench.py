@@ -6,18 +6,22 @@
 One step = one fused forward over one batch of synthetic N(0,1) inputs already
 resident in HBM. Default workload (per GPU): the kernel-only configuration
 B=4, H_q=32, H_k=8, T=8192, d=128, L=32, chunk 64, bf16. With N GPUs each rank
-runs its own shard of a 4N-batch (units = batch x KV head), no data-path
-collective ("scaling": "weak"); NCCL only gathers output checksums to rank 0
-for verification. ``--workload scaling`` runs the multi-GPU configuration
-(B=16, H_q=64, H_k=8, T=16384, d=128, L=48, chunk 128) split by batch over the
-ranks ("scaling": "strong").
+runs its own 4-batch, no data-path collective ("scaling": "weak"); NCCL only
+gathers verification results to rank 0. ``--workload scaling`` makes the
+multi-GPU configuration (B=16, H_q=64, H_k=8, T=16384, d=128, L=48, chunk 128)
+the headline instead, its 128 (batch x KV head) units split over the ranks
+("scaling": "strong").
 
 The JSON line carries: value (aggregate TFLOP/s), roofline (dominant kernel,
 CUDA-event timed, against MEASURED_PEAKS.json), e2e (same metric through the
 public API with pinned host buffers and H2D/D2H copies inside the timed
-region), cpu_baseline (the numpy oracle port of moda_attention_naive timed on
-this host on a bounded sample), clocks sampled during the timed region, and
-gpu_launches. ``--impl reference`` times that CPU port alone on rank 0.
+region), cpu_baseline (the reference's own moda_attention_naive, torch on the
+host CPU, timed on one (batch, KV head) unit), clocks sampled during the timed
+region, gpu_launches, verify (every rank's sampled output rows against a float64
+restatement, pass/fail per rank; the run exits 1 if any fails) and
+multi_gpu_config: the multi-GPU configuration split by units over the same N
+ranks (strong scaling), timed as the max over ranks, with its own row check.
+``--impl reference`` times the CPU baseline alone on rank 0.
 
 ``--pass model`` (one GPU) times the full MoDAModel forward of the model
 configuration (d_model 2048, 16 query / 4 KV heads of 128, 24 layers, post-norm,
@@ -72,7 +76,7 @@ WORKLOADS = {
                            "L=32 chunk_size=64 (profiling size)"),
     "scaling": dict(B=16, Hq=64, Hk=8, T=16384, d=128, L=48, chunk=128, seed=4,
                     desc="multi-GPU fused MoDA forward, bf16: B=16 H_q=64 H_k=8 T=16384 d=128 "
-                         "L=48 chunk_size=128, batch split over GPUs"),
+                         "L=48 chunk_size=128, (batch x kv-head) units split over GPUs"),
 }
 METRIC = "MoDA fused seq+depth attention forward throughput (TFLOP/s)"
 METRIC_BWD = "MoDA fused seq+depth attention backward throughput (TFLOP/s)"
@@ -265,6 +269,140 @@ def make_inputs(wl, b_lo, b_hi, device, dtype):
     return Q, K, V, Kd, Vd
 
 
+def make_unit_inputs(wl, u_lo, u_hi, device, dtype):
+    """Seeded inputs for (batch x KV head) units [u_lo, u_hi) as a problem of
+    U = u_hi - u_lo batches with G query heads and one KV head: [U, G, T, d],
+    [U, 1, T, d], [U, 1, T*L, d]. In the contiguous [B, H, rows, d] layouts these are
+    the same bytes as units u = b*H_k + h_k. Unit u uses generator seed
+    (seed*1000003 + u), so any split over GPUs sees the same tensors."""
+    import torch
+    U = u_hi - u_lo
+    G = wl["Hq"] // wl["Hk"]
+    T, d, L = wl["T"], wl["d"], wl["L"]
+    Q = torch.empty(U, G, T, d, device=device, dtype=dtype)
+    K = torch.empty(U, 1, T, d, device=device, dtype=dtype)
+    V = torch.empty_like(K)
+    Kd = torch.empty(U, 1, T * L, d, device=device, dtype=dtype)
+    Vd = torch.empty_like(Kd)
+    for i, u in enumerate(range(u_lo, u_hi)):
+        g = torch.Generator(device=device).manual_seed(wl["seed"] * 1000003 + u)
+        for t in (Q, K, V, Kd, Vd):
+            t[i].normal_(generator=g)
+    return Q, K, V, Kd, Vd
+
+
+def sample_rows(B, Hq, T, G, seed, extra=10):
+    """Rows (b, h, t) to check: first and last tokens, query-tile edges (128/G tokens per
+    tile: the last token of one tile and the first of the next, at 16k-1 boundaries),
+    and seeded random ones."""
+    import random
+    n_tok = max(1, 128 // G)
+    rng = random.Random(seed)
+    rows = [(0, 0, 0), (B - 1, Hq - 1, T - 1), (0, Hq - 1, min(T - 1, n_tok - 1)),
+            (B - 1, 0, min(T - 1, n_tok)), (B // 2, Hq // 2, min(T - 1, 2 * n_tok - 1)),
+            (0, 1 % Hq, min(T - 1, 255)), (B - 1, Hq // 3, min(T - 1, 16 * 97 - 1))]
+    rows += [(rng.randrange(B), rng.randrange(Hq), rng.randrange(T)) for _ in range(extra)]
+    return rows
+
+
+def check_rows(O, Q, K, V, Kd, Vd, L, rows, tol=2e-2):
+    """Output rows of the fused kernel against a float64 restatement of
+    moda_attention_naive (moda/kernels/moda_naive.py:13-97) computed with torch on the
+    same device from the same bf16 inputs: scores of query (b, h, t) against keys
+    [0, t] of KV head h // G and depth rows [t*L, (t+1)*L), one softmax, weights times
+    the matching values. Returns (all rows within tol, largest difference)."""
+    import torch
+    G = Q.shape[1] // K.shape[1]
+    d = Q.shape[3]
+    worst = 0.0
+    for (b, h, t) in rows:
+        hk = h // G
+        keys = torch.cat([K[b, hk, :t + 1], Kd[b, hk, t * L:(t + 1) * L]]).double()
+        vals = torch.cat([V[b, hk, :t + 1], Vd[b, hk, t * L:(t + 1) * L]]).double()
+        p = torch.softmax(keys @ Q[b, h, t].double() * d ** -0.5, dim=0)
+        ref = p @ vals
+        worst = max(worst, float((O[b, h, t].double() - ref).abs().max()))
+    return worst <= tol, worst
+
+
+def time_steps(step, steps, dev, world, stream, clocks=None):
+    """Device time of `steps` calls of step() on `stream` (CUDA events, barrier and
+    synchronize on both sides); returns (this rank's ms, max over ranks ms)."""
+    import torch
+    import torch.distributed as dist
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    ms_local = ev0.elapsed_time(ev1)
+    t = torch.tensor([ms_local], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return ms_local, float(t.item())
+
+
+def run_scaling_config(args, world, rank, dev, stream):
+    """The multi-GPU configuration (B=16, H_q=64, H_k=8, T=16384, d=128, L=48, chunk 128)
+    split over the ranks by (batch x KV head) units (strong scaling: the 128 units are
+    fixed, each rank runs its contiguous share as one launch). Returns the sub-object
+    of the JSON line (rank 0) or None."""
+    import torch
+    from moda.kernels.moda_cuda import moda_forward_into
+    from moda.sharding import unit_shard
+    wl = WORKLOADS["scaling"]
+    Hq, Hk, T, d, L, C = wl["Hq"], wl["Hk"], wl["T"], wl["d"], wl["L"], wl["chunk"]
+    G = Hq // Hk
+    units = wl["B"] * Hk
+    r = unit_shard(units, world, rank)
+    Q, K, V, Kd, Vd = make_unit_inputs(wl, r.start, r.stop, dev, torch.bfloat16)
+    O = torch.empty_like(Q)
+
+    def step():
+        moda_forward_into(O, Q, K, V, Kd, Vd, L, None, C)
+
+    for _ in range(3):
+        step()
+    steps = max(1, min(args.steps, 10))
+    ms_local, ms_max = time_steps(step, steps, dev, world, stream)
+    ok, worst = (check_rows(O, Q, K, V, Kd, Vd, L, sample_rows(len(r), G, T, G, 4 + rank, extra=6))
+                 if len(r) else (True, 0.0))
+    flag = torch.tensor([1.0 if ok else 0.0, worst, float(len(r))], device=dev, dtype=torch.float64)
+    flags = [flag]
+    if world > 1:
+        import torch.distributed as dist
+        flags = [torch.zeros_like(flag) for _ in range(world)]
+        dist.all_gather(flags, flag)
+    del Q, K, V, Kd, Vd, O
+    torch.cuda.empty_cache()
+    ms_step = ms_max / steps
+    f_all = flops(wl["B"], Hq, T, d, L)
+    by_all = hbm_bytes(wl["B"], Hq, Hk, T, d, L)
+    p_tflops, p_gbs, p_kind = peaks()
+    per_gpu = f_all / world / (ms_step * 1e-3) / 1e12
+    t_roof_gpu = max(f_all / world / (p_tflops * 1e12), by_all / world / (p_gbs * 1e9))
+    return {
+        "workload": wl["desc"],
+        "units": units, "units_per_rank": [int(f[2].item()) for f in flags],
+        "scaling": "strong", "steps": steps, "warmup": 3,
+        "ms_per_step": ms_step, "ms_per_step_this_rank0": ms_local / steps,
+        "value": f_all / (ms_step * 1e-3) / 1e12, "unit": "TFLOP/s",
+        "per_gpu_tflops": per_gpu, "tokens_per_s": wl["B"] * T / (ms_step * 1e-3),
+        "tokens_per_s_per_gpu": wl["B"] * T / world / (ms_step * 1e-3),
+        "roofline_frac_per_gpu": t_roof_gpu / (ms_step * 1e-3), "peak_kind": p_kind,
+        "verify": {"rows_ok_per_rank": [bool(f[0].item() == 1.0) for f in flags],
+                   "max_abs_diff_per_rank": [float(f[1].item()) for f in flags],
+                   "tolerance": 2e-2},
+    }
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -274,6 +412,8 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="kernel")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-scaling-config", action="store_true",
+                    help="skip the strong-scaling multi-GPU configuration sub-object")
     ap.add_argument("--pass", dest="which",
                     choices=["forward", "backward", "model", "proj", "triton-reference", "module"],
                     default="forward")
@@ -318,13 +458,25 @@ def main():
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
 
-    # shard: weak scaling gives every rank its own 4-batch; strong scaling splits 16 batches
-    shard = shard_batches(wl["B"], world, rank, weak=args.workload != "scaling")
-    b_lo, b_hi, B_global = shard.b_lo, shard.b_hi, shard.global_batch
-    B = shard.batch
+    # shard: the kernel-only workload gives every rank its own 4-batch (weak scaling);
+    # --workload scaling splits the 128 (batch x KV head) units of the multi-GPU
+    # configuration over the ranks (strong scaling, one launch per rank)
     Hq, Hk, T, d, L, C = wl["Hq"], wl["Hk"], wl["T"], wl["d"], wl["L"], wl["chunk"]
     dtype = torch.bfloat16
-    Q, K, V, Kd, Vd = make_inputs(wl, b_lo, b_hi, dev, dtype)
+    strong = args.workload == "scaling"
+    if strong:
+        from moda.sharding import unit_shard
+        ur = unit_shard(wl["B"] * Hk, world, rank)
+        Q, K, V, Kd, Vd = make_unit_inputs(wl, ur.start, ur.stop, dev, dtype)
+        B_global = wl["B"]
+        f_rank = flops(len(ur), Hq // Hk, T, d, L)
+        by_rank = hbm_bytes(len(ur), Hq // Hk, 1, T, d, L)
+    else:
+        shard = shard_batches(wl["B"], world, rank, weak=True)
+        B_global = shard.global_batch
+        Q, K, V, Kd, Vd = make_inputs(wl, shard.b_lo, shard.b_hi, dev, dtype)
+        f_rank = flops(shard.batch, Hq, T, d, L)
+        by_rank = hbm_bytes(shard.batch, Hq, Hk, T, d, L)
     O = torch.empty_like(Q)
     stream = torch.cuda.current_stream(dev)
 
@@ -333,34 +485,16 @@ def main():
 
     for _ in range(args.warmup):
         step()
-    torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize(dev)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
-        ev0.record(stream)
-        for _ in range(args.steps):
-            step()
-        ev1.record(stream)
-        torch.cuda.synchronize(dev)
+        ms_local, ms_total = time_steps(step, args.steps, dev, world, stream)
         # keep the clock record meaningful when the timed region was shorter than a sample
         if len(clocks.samples) < 3 and clocks.nv:
             t_end = time.time() + 0.6
             while time.time() < t_end:
                 step()
             torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
-    ms_local = ev0.elapsed_time(ev1)
-    ms_t = torch.tensor([ms_local], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
-    ms_total = float(ms_t.item())
     ms_step = ms_total / args.steps
 
-    f_rank = flops(B, Hq, T, d, L)
-    by_rank = hbm_bytes(B, Hq, Hk, T, d, L)
     f_all = flops(B_global, Hq, T, d, L)
     tflops = f_all / (ms_step * 1e-3) / 1e12
     tokens = B_global * T / (ms_step * 1e-3)
@@ -369,9 +503,16 @@ def main():
     achieved = f_rank / (launch_ms * 1e-3) / 1e12
     t_roof = max(f_rank / (p_tflops * 1e12), by_rank / (p_gbs * 1e9))
 
-    # verification gather (NCCL, outside the timed region): per-rank output checksums
-    gathered = gather_checksums(output_checksum(O))
+    # verification (outside the timed region): every rank checks sampled output rows
+    # against a float64 restatement; NCCL gathers the pass/fail flags and checksums
+    G = Hq // Hk
+    rows_ok, worst = check_rows(O, Q, K, V, Kd, Vd, L,
+                                sample_rows(O.shape[0], O.shape[1], T, G, 100 + rank))
+    cs = torch.cat([output_checksum(O),
+                    torch.tensor([1.0 if rows_ok else 0.0, worst], device=dev, dtype=torch.float64)])
+    gathered = gather_checksums(cs)
     finite_all = all(bool(g[2].item() == 1.0) for g in gathered)
+    rows_ok_all = [bool(g[3].item() == 1.0) for g in gathered]
     status = device_status(dev)
 
     # e2e through the public API: pinned host inputs -> device -> kernel -> host output
@@ -409,6 +550,12 @@ def main():
                "steps": e_steps}
         del bufs, hosts, h_out
 
+    scaling_cfg = None
+    if not strong and not args.no_scaling_config:
+        del Q, K, V, Kd, Vd, O
+        torch.cuda.empty_cache()
+        scaling_cfg = run_scaling_config(args, world, rank, dev, stream)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         c_tf, c_sec, c_desc, c_threads, c_kind = cpu_sample_run(wl, steps=3, warmup=1)
@@ -427,12 +574,14 @@ def main():
     line = {
         "metric": METRIC, "value": tflops, "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
-        "higher_is_better": True, "scaling": "strong" if args.workload == "scaling" else "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic N(0,1), seeded per batch",
+        "higher_is_better": True, "scaling": "strong" if strong else "weak",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic N(0,1), seeded per " + ("unit" if strong else "batch"),
         "config": {"workload": wl["desc"], "global_batch": B_global, "H_q": Hq, "H_k": Hk,
                    "seq_len": T, "head_dim": d, "num_layers": L, "chunk_size": C,
-                   "parallelism": f"{world} GPU(s), (batch x kv-head) units sharded, no collective "
-                                  "in the data path",
+                   "parallelism": f"{world} GPU(s), " + (
+                       "the 128 (batch x kv-head) units split over the ranks" if strong else
+                       "each rank its own 4-batch") + ", no collective in the data path",
                    "l2": "inputs ~%.1f GB per GPU > 126 MB L2 (no flush needed)" % (by_rank / 1e9)},
         "tokens_per_s": tokens,
         "hbm_gbs": by_rank * world / (ms_step * 1e-3) / 1e9,
@@ -446,10 +595,19 @@ def main():
         "cpu_baseline": cpu,
         "gpu_launches": args.steps,
         "clocks": clocks.summary(),
-        "verify": {"finite": finite_all, "device_status": status,
+        "verify": {"ok": bool(finite_all and all(rows_ok_all) and status == 0),
+                   "finite": finite_all, "device_status": status,
+                   "rows_ok_per_rank": rows_ok_all,
+                   "max_abs_diff_per_rank": [float(g[4].item()) for g in gathered],
+                   "tolerance": 2e-2,
                    "checksums": [float(g[0].item()) for g in gathered]},
+        "multi_gpu_config": scaling_cfg,
     }
     print(json.dumps(line), flush=True)
+    ok = line["verify"]["ok"] and (scaling_cfg is None or all(scaling_cfg["verify"]["rows_ok_per_rank"]))
+    if not ok:
+        print("bench: output verification failed", file=sys.stderr)
+        sys.exit(1)
 
 
 def run_backward(args, wl):

@@ -41,10 +41,25 @@ def shard_batches(batch: int, world: int, rank: int, weak: bool) -> BatchShard:
     return BatchShard(rank * per, (rank + 1) * per, batch)
 
 
+def unit_shard(units: int, world: int, rank: int) -> range:
+    """Contiguous range of (batch x KV head) units of `rank`, for any world size: the
+    first ``units % world`` ranks get one unit more than the others.
+
+    Unit u = b * H_k + h_k owns Q[b, h_k*G:(h_k+1)*G], K/V[b, h_k] and the depth rows
+    [b, h_k, :T*L]. In the contiguous [B, H, rows, d] layouts these are consecutive
+    memory, so a contiguous unit range is one slice of every tensor and can be run as a
+    problem of ``len(range)`` batches with G query heads and one KV head.
+    """
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"bad rank {rank} of world {world}")
+    if units < 0:
+        raise ValueError(f"negative unit count {units}")
+    return range(rank * units // world, (rank + 1) * units // world)
+
+
 def unit_ranges(batch: int, kv_heads: int, world: int) -> list[range]:
-    """(batch x KV head) unit ranges per rank for an even batch split (strong scaling)."""
-    per = batch // world
-    return [range(r * per * kv_heads, (r + 1) * per * kv_heads) for r in range(world)]
+    """(batch x KV head) unit ranges of all ranks (strong scaling over any world size)."""
+    return [unit_shard(batch * kv_heads, world, r) for r in range(world)]
 
 
 def output_checksum(O: torch.Tensor) -> torch.Tensor:

@@ -58,3 +58,27 @@ def test_reference_arm_two_ranks_rank0_only():
     lines = _json_lines(r.stdout)
     assert len(lines) == 1
     _check_reference_line(lines[0], 2)
+
+
+def test_row_checker_accepts_the_oracle_and_rejects_a_planted_error():
+    """bench.py's per-rank row check (float64 restatement in torch) agrees with the
+    oracle on small seeded inputs, and catches one wrong output row."""
+    import numpy as np
+    import torch
+    sys.path.insert(0, REPO)
+    import bench
+    from oracle import moda_oracle as orc
+    from helpers import seeded_inputs
+    B, Hq, Hk, T, d, L = 2, 8, 2, 40, 16, 3
+    arrs = seeded_inputs(B, Hq, Hk, T, d, L, seed=5)
+    O = torch.from_numpy(orc.moda_attention_naive(*[a.astype(np.float64) for a in arrs], L))
+    ts = [torch.from_numpy(a) for a in arrs]
+    rows = bench.sample_rows(B, Hq, T, Hq // Hk, seed=1)
+    assert all(0 <= b < B and 0 <= h < Hq and 0 <= t < T for b, h, t in rows)
+    ok, worst = bench.check_rows(O, *ts, L, rows, tol=1e-9)
+    assert ok and worst < 1e-9
+    bad = O.clone()
+    b, h, t = rows[3]
+    bad[b, h, t, 0] += 0.05
+    ok, worst = bench.check_rows(bad, *ts, L, rows)
+    assert not ok and abs(worst - 0.05) < 1e-6

@@ -256,3 +256,73 @@ def test_scaling_config_one_batch_sampled_rows():
                            Kd[b, hk, t * L:(t + 1) * L].cpu().double().numpy(),
                            Vd[b, hk, t * L:(t + 1) * L].cpu().double().numpy(), d ** -0.5)
         assert max_abs(out[b, h, t].float().cpu().numpy(), ref) <= BF16_ABS_TOL, (b, h, t)
+
+
+def _boundary_rows(B, Hq, T, G, L, seed, n_random=16):
+    """First/last tokens, query-tile edges (128/G tokens per tile), 16k-1 tokens, tokens
+    whose depth window [t*L, (t+1)*L) straddles a 128-row block, and seeded random rows."""
+    n_tok = 128 // G
+    toks = {0, T - 1, n_tok - 1, n_tok, 2 * n_tok - 1, 2 * n_tok, 15, 16 * 7 - 1, 16 * 64 - 1}
+    toks |= {t for t in range(0, min(T, 600)) if (t * L) // 128 != ((t + 1) * L - 1) // 128}
+    toks = sorted(t for t in toks if 0 <= t < T)
+    rng = np.random.default_rng(seed)
+    rows = [(int(rng.integers(B)), int(rng.integers(Hq)), t) for t in toks]
+    rows += [(B - 1, Hq - 1, T - 1), (0, 0, 0)]
+    rows += [(int(rng.integers(B)), int(rng.integers(Hq)), int(rng.integers(T)))
+             for _ in range(n_random)]
+    return rows
+
+
+def _check_sampled(out, Q, K, V, Kd, Vd, L, rows):
+    G = Q.shape[1] // K.shape[1]
+    d = Q.shape[3]
+    for (b, h, t) in rows:
+        hk = h // G
+        ref = orc.moda_row(Q[b, h, t].cpu().double().numpy(), K[b, hk, :t + 1].cpu().double().numpy(),
+                           V[b, hk, :t + 1].cpu().double().numpy(),
+                           Kd[b, hk, t * L:(t + 1) * L].cpu().double().numpy(),
+                           Vd[b, hk, t * L:(t + 1) * L].cpu().double().numpy(), d ** -0.5)
+        assert max_abs(out[b, h, t].float().cpu().numpy(), ref) <= BF16_ABS_TOL, (b, h, t)
+
+
+@pytest.mark.slow
+def test_module_config_kernel_shape_sampled_rows():
+    """The module configuration's kernel call at full size: B=8, H_q=8, H_k=4, T=2048,
+    d=64, L=5 (L not a multiple of 16: the per-score depth mask), Q/K/V as the module
+    passes them (transposed views of [B, T, H, d] projections), depth [8, 4, 10240, 64]."""
+    B, Hq, Hk, T, d, L = 8, 8, 4, 2048, 64, 5
+    g = torch.Generator(device="cuda").manual_seed(1)
+    mk = lambda *s: torch.randn(*s, device="cuda", generator=g, dtype=torch.bfloat16)
+    Q = mk(B, T, Hq, d).transpose(1, 2)
+    K, V = mk(B, T, Hk, d).transpose(1, 2), mk(B, T, Hk, d).transpose(1, 2)
+    Kd, Vd = mk(B, Hk, T * L, d), mk(B, Hk, T * L, d)
+    assert moda_plan(Q, K, V, Kd, Vd, L) == "tc"
+    out = moda_attention_cuda(Q, K, V, Kd, Vd, L, chunk_size=64)
+    assert torch.isfinite(out).all()
+    _check_sampled(out, Q, K, V, Kd, Vd, L, _boundary_rows(B, Hq, T, Hq // Hk, L, seed=3))
+
+
+@pytest.mark.slow
+def test_model_config_kernel_shape_through_depth_cache_sampled_rows():
+    """The model configuration's per-layer kernel call at full size: B=8, H_q=16, H_k=4,
+    T=4096, d=128, read through a real DepthKVCache of 2N = 48 slots per token with
+    num_layers = N = 24, as MoDAModel addresses it (token t reads rows [24t, 24t+24) of
+    the 48-slot buffer). L = 24 is not a multiple of 16: the per-score depth mask, and
+    windows that straddle 128-row blocks."""
+    from moda import DepthKVCache
+    B, Hq, Hk, T, d, N = 8, 16, 4, 4096, 128, 24
+    g = torch.Generator(device="cuda").manual_seed(3)
+    mk = lambda *s: torch.randn(*s, device="cuda", generator=g, dtype=torch.bfloat16)
+    cache = DepthKVCache(B, T, 2 * N, Hk, d, device="cuda", dtype=torch.bfloat16)
+    for slot in range(2 * N):  # every slot written, as after a full forward
+        k = mk(B, T, Hk, d).transpose(1, 2)
+        v = mk(B, T, Hk, d).transpose(1, 2)
+        cache.write(slot, k, v, T)
+    Kd, Vd = cache.read(T)
+    assert Kd.shape[2] == T * 2 * N
+    Q = mk(B, T, Hq, d).transpose(1, 2)
+    K, V = mk(B, T, Hk, d).transpose(1, 2), mk(B, T, Hk, d).transpose(1, 2)
+    assert moda_plan(Q, K, V, Kd, Vd, N) == "tc"
+    out = moda_attention_cuda(Q, K, V, Kd, Vd, N, chunk_size=64)
+    assert torch.isfinite(out).all()
+    _check_sampled(out, Q, K, V, Kd, Vd, N, _boundary_rows(B, Hq, T, Hq // Hk, N, seed=4))

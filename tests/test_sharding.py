@@ -15,7 +15,8 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from moda.sharding import BatchShard, gather_checksums, output_checksum, shard_batches, unit_ranges
+from moda.sharding import (BatchShard, gather_checksums, output_checksum, shard_batches,
+                           unit_ranges, unit_shard)
 
 
 def test_weak_and_strong_batch_shards():
@@ -35,6 +36,29 @@ def test_units_partition_the_scaling_workload(world):
     covered = sorted(u for r in ranges for u in r)
     assert covered == list(range(128))
     assert len({len(r) for r in ranges}) == 1
+
+
+@pytest.mark.parametrize("units,world", [(128, 3), (128, 5), (128, 7), (32, 6), (3, 8), (0, 2)])
+def test_units_partition_any_world_size(units, world):
+    ranges = [unit_shard(units, world, r) for r in range(world)]
+    assert [u for r in ranges for u in r] == list(range(units))  # contiguous, in rank order
+    assert max(map(len, ranges)) - min(map(len, ranges)) <= 1     # balanced
+
+
+def test_unit_slice_is_the_same_memory_as_the_batch_head_view():
+    """A unit range read as [U, G, T, d] is the same bytes as the [B, H, T, d] view."""
+    B, Hk, G, T, d = 3, 4, 2, 5, 8
+    Q = torch.randn(B, Hk * G, T, d)
+    K = torch.randn(B, Hk, T, d)
+    r = unit_shard(B * Hk, 5, 2)
+    Qu = Q.view(B * Hk, G, T, d)[r.start:r.stop]
+    Ku = K.view(B * Hk, 1, T, d)[r.start:r.stop]
+    for i, u in enumerate(r):
+        b, hk = divmod(u, Hk)
+        assert torch.equal(Qu[i], Q[b, hk * G:(hk + 1) * G])
+        assert torch.equal(Ku[i, 0], K[b, hk])
+    with pytest.raises(ValueError):
+        unit_shard(8, 2, 2)
 
 
 def _free_port():
