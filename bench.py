@@ -31,7 +31,9 @@ with the reference's cache lifecycle and again with the opt-in lean one.
 ``--pass proj`` (one GPU) times the fused depth-write projection of one model layer
 (x [B=8, T=4096, 2048] times the stacked k/v depth weights [1024, 2048], written into
 cache slot 5 of a [8, 4, 4096*48, 128] cache) against the same work as two library
-GEMMs plus the append kernel; ``--batch`` shrinks B for profiling.
+GEMMs plus the append kernel, and the layer's fused Q/K/V projection (one GEMM over
+cat(W_q, W_k, W_v) writing head-major Q, K, V) against three library GEMMs;
+``--batch`` shrinks B for profiling.
 
 ``--pass module`` (one GPU) times the standalone MoDAAttention forward of the module
 configuration (d_model 512, 8 query / 4 KV heads of 64, B=8, T=2048, 5 layers of depth
@@ -921,6 +923,18 @@ def run_proj(args):
 
     ms, clk = timed(fused)
     ms_ref, _ = timed(unfused)
+    # the attention's Q/K/V projections of the same layer: one fused GEMM writing the
+    # head-major layout against the three nn.Linear of the reference
+    from moda.kernels.moda_cuda import qkv_proj
+    Hq = MODEL_CONFIG["num_heads"]
+    w_qkv = (torch.randn((Hq + 2 * Hk) * d, D, device=dev, generator=g) / D ** 0.5).to(torch.bfloat16)
+    wq, wk, wv = w_qkv[:Hq * d], w_qkv[Hq * d:(Hq + Hk) * d], w_qkv[(Hq + Hk) * d:]
+    ms_qkv, _ = timed(lambda: qkv_proj(x, w_qkv, Hq, Hk, d))
+    ms_qkv_ref, _ = timed(lambda: (F.linear(x, wq), F.linear(x, wk), F.linear(x, wv)))
+    Qf, Kf, Vf = qkv_proj(x, w_qkv, Hq, Hk, d)
+    qkv_diff = max(float((Qf.float() - F.linear(x, wq).view(B, T, Hq, d).transpose(1, 2).float()).abs().max()),
+                   float((Vf.float() - F.linear(x, wv).view(B, T, Hk, d).transpose(1, 2).float()).abs().max()))
+    flop_qkv = 2.0 * B * T * D * (Hq + 2 * Hk) * d
     k_fused = kc[:, :, slot:T * Lc:Lc].clone()
     unfused()
     torch.cuda.synchronize(dev)
@@ -939,6 +953,14 @@ def run_proj(args):
                      "frac": tflops / p_tflops, "peak_kind": p_kind},
         "unfused": {"ms_per_step": ms_ref, "value": flop / (ms_ref * 1e-3) / 1e12,
                     "what": "two library GEMMs (torch F.linear) + moda_depth_append"},
+        "qkv": {"what": f"moda_qkv_proj: x [{B},{T},{D}] x cat(W_q, W_k, W_v)^T "
+                        f"[{(Hq + 2 * Hk) * d},{D}] written as Q, K, V [B, H, T, d]",
+                "ms_per_step": ms_qkv, "value": flop_qkv / (ms_qkv * 1e-3) / 1e12,
+                "frac": flop_qkv / (ms_qkv * 1e-3) / 1e12 / p_tflops,
+                "unfused_ms_per_step": ms_qkv_ref,
+                "unfused_value": flop_qkv / (ms_qkv_ref * 1e-3) / 1e12,
+                "unfused_what": "three library GEMMs (torch F.linear), outputs viewed as transposes",
+                "max_abs_diff_vs_unfused": qkv_diff},
         "gpu_launches": args.steps,
         "clocks": clk,
         "verify": {"bit_equal_to_unfused": same, "device_status": device_status(dev)},

@@ -170,6 +170,21 @@ int moda_depth_proj_append(const ModaTensor* x, const ModaTensor* w, const ModaT
                            const ModaTensor* v_cache, int layer_idx, int num_layers, int seq_len,
                            int dtype, moda_stream_t stream);
 
+/*
+ * The attention's three input projections as one GEMM whose epilogue writes Q, K and V
+ * head-major: y = x . w^T with x [B,1,T,D] and w [1,1,(H_q+2*H_k)*d,D] (the H_q*d rows
+ * of W_q, then W_k, then W_v);
+ *   q[b,h,t,:] = y[b,t,h*d : (h+1)*d]                     (q [B,H_q,T,d])
+ *   k[b,h,t,:] = y[b,t,(H_q+h)*d : ...], v likewise after k (k, v [B,H_k,T,d]).
+ * Any output strides with unit stride along d (16-byte aligned). bf16/f16 with fp32
+ * accumulation (tcgen05); needs d a multiple of 32 and D a multiple of 8, else
+ * MODA_ERR_UNSUPPORTED before any launch.
+ * Replaces q_proj / k_proj / v_proj and their view(B,T,H,d).transpose(1,2)
+ * (moda/attention.py:77-79).
+ */
+int moda_qkv_proj(const ModaTensor* x, const ModaTensor* w, const ModaTensor* q,
+                  const ModaTensor* k, const ModaTensor* v, int dtype, moda_stream_t stream);
+
 /* Text of the last error on the calling thread ("" if none). Thread-local. */
 const char* moda_last_error(void);
 

@@ -409,13 +409,16 @@ int moda_depth_proj_append(const ModaTensor* x, const ModaTensor* w, const ModaT
     moda::ProjProblem q;
     q.x = *x;
     q.w = *w;
-    q.k_cache = *k_cache;
-    q.v_cache = *v_cache;
+    q.out[0] = *k_cache;
+    q.out[1] = *v_cache;
+    q.out[2] = *v_cache;  // unused (nout = 2)
+    q.nout = 2;
+    q.heads[0] = q.heads[1] = static_cast<int>(Hk);
+    q.heads[2] = 0;
     q.B = static_cast<int>(B);
     q.T = static_cast<int>(T);
     q.D = static_cast<int>(D);
     q.N = static_cast<int>(2 * Hk * d);
-    q.Hk = static_cast<int>(Hk);
     q.d = static_cast<int>(d);
     q.L = num_layers;
     q.slot = layer_idx;
@@ -429,6 +432,67 @@ int moda_depth_proj_append(const ModaTensor* x, const ModaTensor* w, const ModaT
             return fail(MODA_ERR_UNSUPPORTED, "fused depth projection needs D > 0");
         return MODA_OK;
     }
+    cudaGetLastError();
+    char err[256] = "";
+    const int r = moda::launch_proj_append(q, static_cast<cudaStream_t>(stream), err, sizeof(err));
+    if (r != MODA_OK) return fail(r, "%s", err[0] ? err : "projection launch failed");
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(MODA_ERR_LAUNCH, "CUDA launch error: %s", cudaGetErrorString(e));
+    return MODA_OK;
+}
+
+int moda_qkv_proj(const ModaTensor* x, const ModaTensor* w, const ModaTensor* q_out,
+                  const ModaTensor* k_out, const ModaTensor* v_out, int dtype, moda_stream_t stream) {
+    g_err[0] = 0;
+    if (!x || !w || !q_out || !k_out || !v_out) return fail(MODA_ERR_ARG, "null tensor descriptor");
+    if (!dtype_ok(dtype)) return fail(MODA_ERR_DTYPE, "unknown dtype code %d", dtype);
+    const ModaTensor* all[5] = {x, w, q_out, k_out, v_out};
+    for (const ModaTensor* t : all)
+        for (int j = 0; j < 4; ++j)
+            if (t->sizes[j] < 0) return fail(MODA_ERR_SHAPE, "negative size");
+    const int64_t B = x->sizes[0], T = x->sizes[2], D = x->sizes[3];
+    const int64_t Hq = q_out->sizes[1], Hk = k_out->sizes[1], d = q_out->sizes[3];
+    if (x->sizes[1] != 1) return fail(MODA_ERR_SHAPE, "x must be [B, 1, T, D]");
+    if (q_out->sizes[0] != B || q_out->sizes[2] != T)
+        return fail(MODA_ERR_SHAPE, "q must be [B, H_q, T, d] with x's B and T");
+    for (const ModaTensor* o : {k_out, v_out})
+        if (o->sizes[0] != B || o->sizes[1] != Hk || o->sizes[2] != T || o->sizes[3] != d)
+            return fail(MODA_ERR_SHAPE, "k and v must both be [B, H_k, T, d] (d of q)");
+    const int64_t N = (Hq + 2 * Hk) * d;
+    if (w->sizes[0] != 1 || w->sizes[1] != 1 || w->sizes[2] != N || w->sizes[3] != D)
+        return fail(MODA_ERR_SHAPE, "w has shape [%lld,%lld,%lld,%lld], expected [1,1,(H_q+2*H_k)*d = %lld,%lld]",
+                    (long long)w->sizes[0], (long long)w->sizes[1], (long long)w->sizes[2],
+                    (long long)w->sizes[3], (long long)N, (long long)D);
+    if (B > 65535 || T > 0x7fffffff || D > 0x7fffffff || N > 0x7fffffff)
+        return fail(MODA_ERR_SHAPE, "sizes too large");
+    for (const ModaTensor* t : all) {
+        int64_t n = 1;
+        for (int j = 0; j < 4; ++j) n *= t->sizes[j];
+        if (n > 0 && !t->ptr) return fail(MODA_ERR_ARG, "null data pointer");
+    }
+    moda::ProjProblem q;
+    q.x = *x;
+    q.w = *w;
+    q.out[0] = *q_out;
+    q.out[1] = *k_out;
+    q.out[2] = *v_out;
+    q.nout = 3;
+    q.heads[0] = static_cast<int>(Hq);
+    q.heads[1] = q.heads[2] = static_cast<int>(Hk);
+    q.B = static_cast<int>(B);
+    q.T = static_cast<int>(T);
+    q.D = static_cast<int>(D);
+    q.N = static_cast<int>(N);
+    q.d = static_cast<int>(d);
+    q.L = 1;
+    q.slot = 0;
+    q.n_write = static_cast<int>(T);
+    q.dtype = dtype;
+    char why[256];
+    if (!moda::proj_supports(q, why, sizeof(why)))
+        return fail(MODA_ERR_UNSUPPORTED, "fused QKV projection %s", why);
+    if (B * T * N == 0) return MODA_OK;
+    if (D == 0) return fail(MODA_ERR_UNSUPPORTED, "fused QKV projection needs D > 0");
     cudaGetLastError();
     char err[256] = "";
     const int r = moda::launch_proj_append(q, static_cast<cudaStream_t>(stream), err, sizeof(err));

@@ -126,10 +126,21 @@ MODA_DEV bool mbar_test(uint32_t bar, uint32_t parity) {
 // so all roles drain to the common exit (TMEM free) instead of spinning.
 constexpr long long kWaitLimitCycles = 4000000000LL;  // about 2 s at 1.9 GHz
 
+#ifndef MODA_WAIT_SLEEP_NS
+#define MODA_WAIT_SLEEP_NS 20
+#endif
+// Back-off of a waiting warp between polls (nanoseconds): a sleeping warp takes no
+// issue slots from the working warps of its scheduler partition (measured 2-5 % faster
+// forward at the kernel-only shape than polling without a pause).
+MODA_DEV void wait_backoff() {
+    if (MODA_WAIT_SLEEP_NS > 0) __nanosleep(MODA_WAIT_SLEEP_NS);
+}
+
 MODA_DEV bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int site) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
     for (uint32_t i = 1;; ++i) {
+        wait_backoff();
         if (mbar_try_wait(bar, parity)) return true;
         if ((i & 255u) == 0) {
             if (*abort_flag) return false;

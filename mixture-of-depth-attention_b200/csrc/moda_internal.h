@@ -51,20 +51,28 @@ struct TcParams {
     int zero_rows;  // implicit all-zero depth rows per token (score 0, value 0)
 };
 
-// Depth-write projection with the cache append fused (moda_depth_proj_append):
-// x [B, 1, T, D], w [1, 1, N = 2*H_k*d, D], caches [B, H_k, >= T*L, d].
+// Projection GEMM y = x . W^T whose epilogue stores column segments of y into up to
+// three head-major outputs: x [B, 1, T, D], w [1, 1, N, D]; segment s covers columns
+// [seg_start, seg_start + heads[s]*d) and stores row t, head h into
+// out[s][b, h, t*L + slot, :] for t < n_write. moda_depth_proj_append: two outputs (the
+// k and v caches, L = cache layers, slot = layer); moda_qkv_proj: three outputs (Q, K,
+// V in [B, H, T, d], L = 1, slot = 0).
 struct ProjProblem {
-    ModaTensor x, w, k_cache, v_cache;
-    int B, T, D, N, Hk, d, L, slot, n_write;
+    ModaTensor x, w, out[3];
+    int nout;
+    int heads[3];
+    int B, T, D, N, d, L, slot, n_write;
     int dtype;
 };
 
 struct ProjParams {
     CUtensorMap tm_x, tm_w;  // first: 64-byte aligned
-    void* kc;
-    void* vc;
-    long long kc_sb, kc_sh, kc_sr, vc_sb, vc_sh, vc_sr;  // cache strides (elements)
-    int B, T, K, N, Hk, d, Lc, slot, n_write;
+    void* out0;
+    void* out1;
+    void* out2;
+    long long o_sb[3], o_sh[3], o_sr[3];  // output strides (elements)
+    int seg_end[3];                       // exclusive column end of each output's segment
+    int B, T, K, N, d, Lc, slot, n_write;
     int m_tiles_per_batch, n_tiles, num_tiles;
 };
 

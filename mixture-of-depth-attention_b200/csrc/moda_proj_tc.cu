@@ -1,13 +1,19 @@
-// Depth-write projection with the cache append in its epilogue (tcgen05 / TMA / TMEM).
+// Projection GEMM with the head-major scatter in its epilogue (tcgen05 / TMA / TMEM).
 //
-//   y[b, t, :] = x[b, t, :] . W^T          W = [W_k ; W_v], [2*H_k*d, D]
-//   k_cache[b, h, t*L + slot, :] = y[b, t, h*d : (h+1)*d]
-//   v_cache[b, h, t*L + slot, :] = y[b, t, (H_k+h)*d : (H_k+h+1)*d]      for t < n_write
+//   y[b, t, :] = x[b, t, :] . W^T          W [N, D], N = (sum of the outputs' heads) * d
+//   out_s[b, h, t*L + slot, :] = y[b, t, c_s + h*d : c_s + (h+1)*d]     for t < n_write
 //
-// The reference computes the two depth projections with nn.Linear (moda/attention.py:
-// 81-82 for the attention's writes, moda/model.py:78-81 for the FFN's) and copies them
-// into the cache with a strided slice assignment (moda/cache.py:73-74); here one GEMM
-// stores its tiles straight into the cache rows, so y never exists in memory.
+// with c_s the first column of output s. Two uses:
+// * the depth writes (moda_depth_proj_append): W = [W_k; W_v], outputs the k and v
+//   caches, L = the cache's layers, slot = the writing layer. The reference computes
+//   the two depth projections with nn.Linear (moda/attention.py:81-82 for the
+//   attention's writes, moda/model.py:78-81 for the FFN's) and copies them into the
+//   cache with a strided slice assignment (moda/cache.py:73-74);
+// * the attention's input projections (moda_qkv_proj): W = [W_q; W_k; W_v], outputs Q,
+//   K, V in [B, H, T, d] (L = 1, slot = 0), the layout the attention kernel reads; the
+//   reference runs three nn.Linear and views them as transposes (moda/attention.py:77-79).
+// In both, one GEMM stores its tiles straight into the destination rows, so y never
+// exists in memory.
 //
 // Tiling: a CTA tile is 256 rows (tokens of one batch) x 256 columns, K in steps of 64.
 // Both 128-row halves of the A tile share the B tile (two M = 128, N = 256 MMAs per
@@ -167,7 +173,6 @@ __global__ void __launch_bounds__(kPThreads, 1)
         const int q = warp & 3;               // TMEM lane quarter
         const int half = (warp - 2) >> 2;     // accumulator: rows [128*half, +128) of the tile
         const uint32_t t_base = tmem + (static_cast<uint32_t>(q * 32) << 16) + half * kPBN;
-        const int hd = p.Hk * p.d;
         uint32_t tcount = 0;
         for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++tcount) {
             const PTile tl = ptile(p, tile);
@@ -188,13 +193,12 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 }
                 const int n = tl.n0 + c * 32;
                 if (!row_ok || n >= p.N) continue;
-                const bool is_v = n >= hd;
-                const int nn = is_v ? n - hd : n;
+                // the output segment holding column n (32-column chunks never straddle a head)
+                const int sg = n < p.seg_end[0] ? 0 : (n < p.seg_end[1] ? 1 : 2);
+                const int nn = n - (sg == 0 ? 0 : p.seg_end[sg - 1]);
                 const int h = nn / p.d, col = nn % p.d;
-                uint16_t* base = static_cast<uint16_t*>(is_v ? p.vc : p.kc);
-                const long long off = (is_v ? p.vc_sb : p.kc_sb) * tl.b +
-                                      (is_v ? p.vc_sh : p.kc_sh) * h +
-                                      (is_v ? p.vc_sr : p.kc_sr) * crow + col;
+                uint16_t* base = static_cast<uint16_t*>(sg == 0 ? p.out0 : (sg == 1 ? p.out1 : p.out2));
+                const long long off = p.o_sb[sg] * tl.b + p.o_sh[sg] * h + p.o_sr[sg] * crow + col;
                 uint4* dst = reinterpret_cast<uint4*>(base + off);
                 uint32_t pk[16];
 #pragma unroll
@@ -250,14 +254,13 @@ bool proj_supports(const ProjProblem& q, char* why, size_t whylen) {
     };
     if (q.dtype != MODA_BF16 && q.dtype != MODA_F16) return no("needs bf16 or f16");
     if (q.d % 32 != 0) return no("needs head_dim a multiple of 32");
-    if (q.x.strides[3] != 1 || q.w.strides[3] != 1 || q.k_cache.strides[3] != 1 ||
-        q.v_cache.strides[3] != 1)
-        return no("needs unit stride along the feature dimension");
-    const ModaTensor* ts[4] = {&q.x, &q.w, &q.k_cache, &q.v_cache};
-    for (const ModaTensor* t : ts) {
+    const ModaTensor* ts[5] = {&q.x, &q.w, &q.out[0], &q.out[1], &q.out[2]};
+    for (int i = 0; i < 2 + q.nout; ++i) {
+        const ModaTensor* t = ts[i];
+        if (t->strides[3] != 1) return no("needs unit stride along the feature dimension");
         if (reinterpret_cast<uintptr_t>(t->ptr) % 16 != 0) return no("needs 16-byte aligned tensors");
-        for (int i = 0; i < 3; ++i)
-            if (t->sizes[i] > 1 && (t->strides[i] * 2) % 16 != 0)
+        for (int j = 0; j < 3; ++j)
+            if (t->sizes[j] > 1 && (t->strides[j] * 2) % 16 != 0)
                 return no("needs 16-byte multiple strides");
     }
     if (q.D % 8 != 0) return no("needs D a multiple of 8");
@@ -271,19 +274,27 @@ int launch_proj_append(const ProjProblem& q, cudaStream_t stream, char* err, siz
     if (!encode_map(&p.tm_x, q.x, q.T, false, 2, dt, kPBM, 1, err, errlen, "x") ||
         !encode_map(&p.tm_w, q.w, q.N, false, 2, dt, kPBN, 1, err, errlen, "W"))
         return MODA_ERR_LAUNCH;
-    p.kc = q.k_cache.ptr;
-    p.vc = q.v_cache.ptr;
-    p.kc_sb = q.k_cache.strides[0];
-    p.kc_sh = q.k_cache.strides[1];
-    p.kc_sr = q.k_cache.strides[2];
-    p.vc_sb = q.v_cache.strides[0];
-    p.vc_sh = q.v_cache.strides[1];
-    p.vc_sr = q.v_cache.strides[2];
+    void* outs[3] = {nullptr, nullptr, nullptr};
+    int end = 0;
+    for (int i = 0; i < 3; ++i) {
+        if (i < q.nout) {
+            outs[i] = q.out[i].ptr;
+            p.o_sb[i] = q.out[i].strides[0];
+            p.o_sh[i] = q.out[i].strides[1];
+            p.o_sr[i] = q.out[i].strides[2];
+            end += q.heads[i] * q.d;
+        } else {
+            p.o_sb[i] = p.o_sh[i] = p.o_sr[i] = 0;
+        }
+        p.seg_end[i] = end;  // a missing segment is empty (end repeats)
+    }
+    p.out0 = outs[0];
+    p.out1 = outs[1];
+    p.out2 = outs[2];
     p.B = q.B;
     p.T = q.T;
     p.K = q.D;
     p.N = q.N;
-    p.Hk = q.Hk;
     p.d = q.d;
     p.Lc = q.L;
     p.slot = q.slot;

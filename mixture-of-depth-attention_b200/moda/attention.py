@@ -14,7 +14,8 @@ import torch.nn as nn
 from torch import Tensor
 
 from .config import MoDAConfig
-from .kernels.moda_cuda import moda_attention_cuda, moda_attention_zero_depth
+from .kernels._lib import MoDAUnsupported
+from .kernels.moda_cuda import moda_attention_cuda, moda_attention_zero_depth, qkv_proj
 
 
 class MoDAAttention(nn.Module):
@@ -42,6 +43,33 @@ class MoDAAttention(nn.Module):
                                       bias=False)
         self.use_triton = False  # kept for API parity; there is one CUDA path
         self.dropout = nn.Dropout(config.dropout) if config.dropout > 0 else nn.Identity()
+        self._w_qkv = None      # cat(W_q, W_k, W_v) for the fused projection, and the
+        self._w_qkv_key = None  # weights' (pointer, version) it was built from
+
+    def _fused_qkv_weight(self) -> Tensor:
+        ws = (self.q_proj.weight, self.k_proj.weight, self.v_proj.weight)
+        key = tuple((w.data_ptr(), w._version, w.dtype, w.device) for w in ws)
+        if self._w_qkv is None or self._w_qkv_key != key:
+            self._w_qkv = torch.cat([w.detach() for w in ws], dim=0)
+            self._w_qkv_key = key
+        return self._w_qkv
+
+    def _project_qkv(self, x: Tensor) -> tuple[Tensor, Tensor, Tensor]:
+        """Q, K, V as [B, H, T, d]. Without autograd: one fused GEMM (moda_qkv_proj)
+        writing the head-major layout; otherwise (or where that kernel does not take the
+        shape) the three nn.Linear of the reference, viewed as transposes (same values)."""
+        B, T, _ = x.shape
+        H_q, H_k, d = self.num_heads, self.num_kv_heads, self.head_dim
+        if not torch.is_grad_enabled() and x.is_cuda and x.dtype in (torch.bfloat16, torch.float16):
+            try:
+                return qkv_proj(x.contiguous(), self._fused_qkv_weight(), H_q, H_k, d)
+            except MoDAUnsupported:
+                pass
+        # [B, H, T, d] views with strides (T*H*d, d, H*d, 1): the kernel reads them in place
+        Q = self.q_proj(x).view(B, T, H_q, d).transpose(1, 2)
+        K = self.k_proj(x).view(B, T, H_k, d).transpose(1, 2)
+        V = self.v_proj(x).view(B, T, H_k, d).transpose(1, 2)
+        return Q, K, V
 
     def forward(self, x: Tensor, K_depth: Optional[Tensor] = None,
                 V_depth: Optional[Tensor] = None, *, zero_depth_rows: int = 0,
@@ -65,10 +93,7 @@ class MoDAAttention(nn.Module):
         """
         B, T, D = x.shape
         H_q, H_k, d = self.num_heads, self.num_kv_heads, self.head_dim
-        # [B, H, T, d] views with strides (T*H*d, d, H*d, 1): the kernel reads them in place
-        Q = self.q_proj(x).view(B, T, H_q, d).transpose(1, 2)
-        K = self.k_proj(x).view(B, T, H_k, d).transpose(1, 2)
-        V = self.v_proj(x).view(B, T, H_k, d).transpose(1, 2)
+        Q, K, V = self._project_qkv(x)
         n_w = T if write_tokens is None else max(0, min(int(write_tokens), T))
         if n_w > 0:
             # projected over all T tokens: a token slice of a batched x is strided and

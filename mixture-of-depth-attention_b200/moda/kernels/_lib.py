@@ -22,7 +22,7 @@ MODA_ERR_DTYPE, MODA_ERR_LAUNCH, MODA_ERR_UNSUPPORTED = -4, -5, -6
 KERNEL_AUTO, KERNEL_TC, KERNEL_SIMT = 0, 1, 2
 
 EXPORTED_SYMBOLS = ("moda_fwd", "moda_fwd_ex", "moda_fwd_lse", "moda_fwd_zero_depth",
-                    "moda_fwd_plan", "moda_bwd", "moda_depth_proj_append",
+                    "moda_fwd_plan", "moda_bwd", "moda_depth_proj_append", "moda_qkv_proj",
                     "moda_bwd_noalloc", "moda_bwd_workspace_size", "moda_depth_append",
                     "moda_last_error", "moda_device_status", "moda_version")
 NOALLOC_ROWS = 1 << 20   # MODA_NOALLOC_ROWS
@@ -84,6 +84,8 @@ def load():
         lib.moda_depth_append.restype = i
         lib.moda_depth_proj_append.argtypes = [T, T, T, T, i, i, i, i, vp]
         lib.moda_depth_proj_append.restype = i
+        lib.moda_qkv_proj.argtypes = [T, T, T, T, T, i, vp]
+        lib.moda_qkv_proj.restype = i
         lib.moda_last_error.argtypes = []
         lib.moda_last_error.restype = ctypes.c_char_p
         lib.moda_device_status.argtypes = [vp]

@@ -314,6 +314,40 @@ def depth_proj_append(x: Tensor, w_kv: Tensor, k_cache: Tensor, v_cache: Tensor,
     _lib.check(code, "moda_depth_proj_append")
 
 
+def qkv_proj(x: Tensor, w_qkv: Tensor, num_heads: int, num_kv_heads: int,
+             head_dim: int) -> tuple[Tensor, Tensor, Tensor]:
+    """The attention's three input projections as one kernel (moda/attention.py:77-79).
+
+    x [B, T, D]; w_qkv [(H_q + 2*H_k)*d, D] = cat(W_q, W_k, W_v). Returns Q [B, H_q, T, d],
+    K, V [B, H_k, T, d], contiguous (the layout the attention kernel reads; the
+    reference's transposed views hold the same values). No autograd. Raises
+    ``MoDAUnsupported`` (before any launch) for fp32, d not a multiple of 32, D not a
+    multiple of 8 or unaligned layouts.
+    """
+    for n, t in (("x", x), ("w_qkv", w_qkv)):
+        if t.device.type != "cuda":
+            raise RuntimeError(f"QKV projection runs on CUDA tensors only ({n} is on {t.device})")
+        if t.device != x.device:
+            raise RuntimeError(f"{n} is on {t.device}, x on {x.device}")
+        if t.dtype != x.dtype:
+            raise TypeError(f"{n} has dtype {t.dtype}, x has {x.dtype}")
+    if x.dim() != 3 or w_qkv.dim() != 2:
+        raise _lib.MoDAShapeError("x must be [B, T, D] and w_qkv [(H_q+2*H_k)*d, D]")
+    if x.dtype not in _DTYPES:
+        raise TypeError(f"unsupported dtype {x.dtype}")
+    B, T, _ = x.shape
+    Q = x.new_empty(B, num_heads, T, head_dim)
+    K = x.new_empty(B, num_kv_heads, T, head_dim)
+    V = x.new_empty(B, num_kv_heads, T, head_dim)
+    lib = _lib.load()
+    stream = torch.cuda.current_stream(x.device).cuda_stream
+    with torch.cuda.device(x.device):
+        code = lib.moda_qkv_proj(_desc(x.unsqueeze(1)), _desc(w_qkv[None, None]), _desc(Q),
+                                 _desc(K), _desc(V), _DTYPES[x.dtype], stream)
+    _lib.check(code, "moda_qkv_proj")
+    return Q, K, V
+
+
 class _DepthAppendFunction(torch.autograd.Function):
     """In-place depth append that autograd sees, like the reference's strided slice
     assignment into the cache (moda/cache.py:73-74, recorded by torch as a copy into

@@ -191,3 +191,21 @@ def test_depth_projection_rejects_before_launch(case):
               "short_cache": _lib.MODA_ERR_DEPTH_ROWS, "slot": _lib.MODA_ERR_ARG}[case]
     assert code == expect
     assert lib.moda_last_error() != b""
+
+
+@pytest.mark.parametrize("case", ["w_rows", "kv_heads", "dtype", "x_heads"])
+def test_qkv_projection_rejects_before_launch(case):
+    """Shape and dtype errors of moda_qkv_proj are found on the host (no launch: the
+    descriptors point at nothing)."""
+    lib = _lib.load()
+    B, T, D, Hq, Hk, d = 2, 16, 64, 4, 2, 32
+    x = _lib.describe(256, (B, 1 if case != "x_heads" else 2, T, D), (T * D, T * D, D, 1))
+    n = (Hq + 2 * Hk) * d + (32 if case == "w_rows" else 0)
+    w = _lib.describe(256, (1, 1, n, D), (n * D, n * D, D, 1))
+    q = _lib.describe(256, (B, Hq, T, d), (Hq * T * d, T * d, d, 1))
+    hk_v = Hk + 1 if case == "kv_heads" else Hk
+    k = _lib.describe(256, (B, Hk, T, d), (Hk * T * d, T * d, d, 1))
+    v = _lib.describe(256, (B, hk_v, T, d), (hk_v * T * d, T * d, d, 1))
+    dtype = 99 if case == "dtype" else _lib.MODA_BF16
+    code = lib.moda_qkv_proj(x, w, q, k, v, dtype, None)
+    assert code == (_lib.MODA_ERR_DTYPE if case == "dtype" else _lib.MODA_ERR_SHAPE)

@@ -96,3 +96,55 @@ def test_fp32_is_refused_before_launch():
     x, w, kc, vc = _case(1, 8, 64, 1, 32, 2, torch.float32)
     with pytest.raises(MoDAUnsupported):
         depth_proj_append(x, w, kc, vc, 0, 2, 8)
+
+
+# ---------------------------------------------------------------- fused Q/K/V projection
+from moda.kernels.moda_cuda import qkv_proj  # noqa: E402
+
+QKV_CASES = [  # B, T, D, H_q, H_k, d
+    (2, 300, 256, 4, 2, 64),       # ragged T
+    (1, 512, 2048, 16, 4, 128),    # the model configuration's heads (N = 3072)
+    (2, 257, 200, 2, 1, 64),       # K tail (D % 64 != 0), N = 256
+    (1, 96, 128, 6, 3, 96),        # d = 96: segment ends inside column tiles
+    (1, 64, 512, 8, 4, 64),        # the module configuration's heads
+]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("case", QKV_CASES, ids=[str(c) for c in QKV_CASES])
+def test_fused_qkv_projection(case, dtype):
+    """One GEMM over cat(W_q, W_k, W_v) writes Q, K, V head-major; each equals the
+    float32 product of the same rounded inputs within the 16-bit output tolerance."""
+    B, T, D, Hq, Hk, d = case
+    g = torch.Generator(device="cuda").manual_seed(3)
+    x = torch.randn(B, T, D, device="cuda", generator=g).to(dtype)
+    w = (torch.randn((Hq + 2 * Hk) * d, D, device="cuda", generator=g) / D ** 0.5).to(dtype)
+    Q, K, V = qkv_proj(x, w, Hq, Hk, d)
+    torch.cuda.synchronize()
+    y = x.float() @ w.float().t()
+    eq = y[..., :Hq * d].view(B, T, Hq, d).transpose(1, 2)
+    ek = y[..., Hq * d:(Hq + Hk) * d].view(B, T, Hk, d).transpose(1, 2)
+    ev = y[..., (Hq + Hk) * d:].view(B, T, Hk, d).transpose(1, 2)
+    for got, exp in ((Q, eq), (K, ek), (V, ev)):
+        assert got.shape == exp.shape and got.is_contiguous()
+        assert (got.float() - exp).abs().max().item() <= TOL
+
+
+def test_module_uses_fused_qkv_without_autograd():
+    """MoDAAttention under no_grad (fused QKV GEMM) and with autograd (three nn.Linear)
+    give the same output within the 16-bit tolerance; the cached concatenated weight
+    follows an in-place weight update."""
+    from moda import MoDAAttention, MoDAConfig
+    torch.manual_seed(0)
+    cfg = MoDAConfig(d_model=256, num_heads=4, num_kv_heads=2, head_dim=64, num_layers=3)
+    attn = MoDAAttention(cfg).cuda().to(torch.bfloat16)
+    x = torch.randn(2, 96, 256, device="cuda", dtype=torch.bfloat16)
+    Kd = torch.randn(2, 2, 96 * 3, 64, device="cuda", dtype=torch.bfloat16)
+    Vd = torch.randn_like(Kd)
+    for _ in range(2):
+        with torch.no_grad():
+            fast = attn(x, Kd, Vd)[0]
+        ref = attn(x, Kd, Vd)[0].detach()
+        assert (fast.float() - ref.float()).abs().max().item() <= TOL
+        with torch.no_grad():
+            attn.k_proj.weight.mul_(0.5)  # bumps the version: the fused weight is rebuilt
