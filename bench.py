@@ -76,6 +76,10 @@ WORKLOADS = {
     "kernel-b1": dict(B=1, Hq=32, Hk=8, T=8192, d=128, L=32, chunk=64, seed=2,
                       desc="kernel-only fused MoDA forward, bf16: B=1 H_q=32 H_k=8 T=8192 d=128 "
                            "L=32 chunk_size=64 (profiling size)"),
+    # the same B=1 case without depth rows (L = 0): the sequence part alone, for ncu
+    "kernel-b1-nodepth": dict(B=1, Hq=32, Hk=8, T=8192, d=128, L=0, chunk=64, seed=2,
+                              desc="causal attention part alone, bf16: B=1 H_q=32 H_k=8 T=8192 "
+                                   "d=128 L=0 (profiling size)"),
     "scaling": dict(B=16, Hq=64, Hk=8, T=16384, d=128, L=48, chunk=128, seed=4,
                     desc="multi-GPU fused MoDA forward, bf16: B=16 H_q=64 H_k=8 T=16384 d=128 "
                          "L=48 chunk_size=128, (batch x kv-head) units split over GPUs"),

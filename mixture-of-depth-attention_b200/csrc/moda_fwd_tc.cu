@@ -166,7 +166,9 @@ __device__ __forceinline__ Fills step_fills(const Step& st, uint32_t base) {
     return r;
 }
 
-template <int HD, int FMT>
+// DG: width of the column groups a depth window is picked by (16, or 8 for L a multiple
+// of 8 but not of 16, so that such L also avoid the per-score depth mask).
+template <int HD, int FMT, int DG>
 __global__ void __launch_bounds__(kThreads, 1) moda_fwd_tc_kernel(const __grid_constant__ TcParams p) {
     using Cfg = TcCfg<HD>;
     extern __shared__ uint8_t smem_raw[];
@@ -535,12 +537,13 @@ __global__ void __launch_bounds__(kThreads, 1) moda_fwd_tc_kernel(const __grid_c
                 lo -= 64 * half;  // into this warp's column range
                 hi -= 64 * half;
                 const bool live = !need_mask || (lo < hi && hi > 0 && lo < 64);
-                // With L a multiple of 16 a depth block's window [lo, hi) covers whole
-                // 16-column groups: pick groups per row instead of masking each score.
-                const bool chunked = st.dep && (p.L & 15) == 0;
-                bool ok[4];
+                // With L a multiple of DG a depth block's window [lo, hi) covers whole
+                // DG-column groups: pick groups per row instead of masking each score.
+                constexpr int kNG = 64 / DG;  // groups in this warp's 64 columns
+                const bool chunked = st.dep && (p.L % DG) == 0;
+                bool ok[kNG];
 #pragma unroll
-                for (int k = 0; k < 4; ++k) ok[k] = lo <= 16 * k && hi >= 16 * k + 16;
+                for (int k = 0; k < kNG; ++k) ok[k] = lo <= DG * k && hi >= DG * k + DG;
                 float mx = -INFINITY;
                 if (__any_sync(0xffffffffu, live)) {
                     if (need_mask && !chunked) {
@@ -556,20 +559,37 @@ __global__ void __launch_bounds__(kThreads, 1) moda_fwd_tc_kernel(const __grid_c
                                 sv[c] = c < hi ? sv[c] : __float_as_uint(-INFINITY);
                         }
                     }
-                    float mx4[4];
+                    if constexpr (DG == 16) {
+                        float mx4[4];
 #pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        float a = __uint_as_float(sv[16 * k]);
+                        for (int k = 0; k < 4; ++k) {
+                            float a = __uint_as_float(sv[16 * k]);
 #pragma unroll
-                        for (int i = 1; i < 15; i += 2)
-                            a = fmax3(a, __uint_as_float(sv[16 * k + i]), __uint_as_float(sv[16 * k + i + 1]));
-                        mx4[k] = fmaxf(a, __uint_as_float(sv[16 * k + 15]));
+                            for (int i = 1; i < 15; i += 2)
+                                a = fmax3(a, __uint_as_float(sv[16 * k + i]), __uint_as_float(sv[16 * k + i + 1]));
+                            mx4[k] = fmaxf(a, __uint_as_float(sv[16 * k + 15]));
+                        }
+                        if (chunked)
+                            mx = fmaxf(fmaxf(ok[0] ? mx4[0] : -INFINITY, ok[1] ? mx4[1] : -INFINITY),
+                                       fmaxf(ok[2] ? mx4[2] : -INFINITY, ok[3] ? mx4[3] : -INFINITY));
+                        else
+                            mx = fmaxf(fmax3(mx4[0], mx4[1], mx4[2]), mx4[3]);
+                    } else {
+                        float m8[8];
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) {
+                            float a = fmax3(__uint_as_float(sv[8 * k]), __uint_as_float(sv[8 * k + 1]),
+                                            __uint_as_float(sv[8 * k + 2]));
+                            a = fmax3(a, __uint_as_float(sv[8 * k + 3]), __uint_as_float(sv[8 * k + 4]));
+                            a = fmax3(a, __uint_as_float(sv[8 * k + 5]), __uint_as_float(sv[8 * k + 6]));
+                            m8[k] = fmaxf(a, __uint_as_float(sv[8 * k + 7]));
+                        }
+                        if (chunked) {
+#pragma unroll
+                            for (int k = 0; k < 8; ++k) m8[k] = ok[k] ? m8[k] : -INFINITY;
+                        }
+                        mx = fmaxf(fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), m8[6]), m8[7]);
                     }
-                    if (chunked)
-                        mx = fmaxf(fmaxf(ok[0] ? mx4[0] : -INFINITY, ok[1] ? mx4[1] : -INFINITY),
-                                   fmaxf(ok[2] ? mx4[2] : -INFINITY, ok[3] ? mx4[3] : -INFINITY));
-                    else
-                        mx = fmaxf(fmax3(mx4[0], mx4[1], mx4[2]), mx4[3]);
                 }
                 // trade partial row maxima with the partner warp (double-buffered by block parity)
                 float* xm = xmax + (nblk & 1u) * 256;
@@ -600,15 +620,19 @@ __global__ void __launch_bounds__(kThreads, 1) moda_fwd_tc_kernel(const __grid_c
                     for (int q4 = 0; q4 < 2; ++q4) {
                         uint32_t pk[16];
                         // a group outside the row's depth window gives exp2(-inf) = 0
-                        const float nba = (chunked && !ok[2 * q4]) ? -INFINITY : -m_base;
-                        const float nbb = (chunked && !ok[2 * q4 + 1]) ? -INFINITY : -m_base;
-                        const uint64_t nma = f2_pack(nba, nba), nmb = f2_pack(nbb, nbb);
+                        constexpr int kGq = 32 / DG;  // groups in these 32 columns
+                        uint64_t nmg[kGq];
+#pragma unroll
+                        for (int k = 0; k < kGq; ++k) {
+                            const float nb = (chunked && !ok[kGq * q4 + k]) ? -INFINITY : -m_base;
+                            nmg[k] = f2_pack(nb, nb);
+                        }
 #pragma unroll
                         for (int c = 0; c < 32; c += 2) {
                             const int cc = 32 * q4 + c;
                             const uint64_t xx = f2_fma(
                                 f2_pack(__uint_as_float(sv[cc]), __uint_as_float(sv[cc + 1])), sc2,
-                                c < 16 ? nma : nmb);
+                                nmg[c / DG]);
                             float x0, x1;
                             f2_unpack(xx, x0, x1);
                             const float p0 = ex2(x0), p1 = ex2(x1);
@@ -814,10 +838,10 @@ bool tc_supports(const FwdParams& p, char* why, size_t whylen) {
     return true;
 }
 
-template <int HD, int FMT>
+template <int HD, int FMT, int DG>
 static int launch_tc_inst(const TcParams& tp, int grid, cudaStream_t stream) {
     using Cfg = TcCfg<HD>;
-    auto kern = moda_fwd_tc_kernel<HD, FMT>;
+    auto kern = moda_fwd_tc_kernel<HD, FMT, DG>;
     static std::atomic<uint64_t> attr_done{0};
     static std::atomic<int> num_regs{0};  // registers per thread of the compiled kernel, once known
     int nr = num_regs.load(std::memory_order_relaxed);
@@ -880,10 +904,17 @@ int launch_fwd_tc(const FwdParams& p, cudaStream_t stream, char* err, size_t err
     }
     tp.num_items = static_cast<int>(items);
     const int g = static_cast<int>(items < sm_count() ? items : sm_count());
-    if (p.d == 128) return p.dtype == MODA_BF16 ? launch_tc_inst<128, 1>(tp, g, stream)
-                                                : launch_tc_inst<128, 0>(tp, g, stream);
-    return p.dtype == MODA_BF16 ? launch_tc_inst<64, 1>(tp, g, stream)
-                                : launch_tc_inst<64, 0>(tp, g, stream);
+    // 8-column depth groups only where 16 would not divide L: finer groups cost every
+    // block a little (more group maxima and biases), so L % 16 == 0 keeps 16.
+    const bool g8 = p.L % 16 != 0 && p.L % 8 == 0;
+    if (p.d == 128) {
+        if (p.dtype == MODA_BF16)
+            return g8 ? launch_tc_inst<128, 1, 8>(tp, g, stream) : launch_tc_inst<128, 1, 16>(tp, g, stream);
+        return g8 ? launch_tc_inst<128, 0, 8>(tp, g, stream) : launch_tc_inst<128, 0, 16>(tp, g, stream);
+    }
+    if (p.dtype == MODA_BF16)
+        return g8 ? launch_tc_inst<64, 1, 8>(tp, g, stream) : launch_tc_inst<64, 1, 16>(tp, g, stream);
+    return g8 ? launch_tc_inst<64, 0, 8>(tp, g, stream) : launch_tc_inst<64, 0, 16>(tp, g, stream);
 }
 
 }  // namespace moda

@@ -90,6 +90,11 @@ SHAPES = [
     (1, 4, 2, 45, 64, 96),
     (1, 32, 2, 50, 128, 32),
     (1, 32, 1, 20, 64, 32),
+    # L a multiple of 8 but not of 16: 8-column depth groups (windows straddle blocks)
+    (1, 16, 4, 300, 128, 24),
+    (2, 8, 2, 133, 64, 40),
+    (1, 4, 4, 70, 128, 8),
+    (1, 64, 8, 45, 64, 56),
 ]
 
 
