@@ -718,6 +718,36 @@ def run_model(args):
             print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=12,
                                             max_name_column_width=60), file=sys.stderr)
     model.config.lean_depth_cache = False
+    # one layer's fused attention call alone, as the model makes it: Q/K/V of the layer's
+    # shape and the depth rows read through a 2N-slot cache with L = N (B=8, H_q=16,
+    # H_k=4, T=4096, d=128, L=24)
+    from moda import DepthKVCache
+    from moda.kernels.moda_cuda import moda_forward_into
+    N, Hq, Hk, d = MODEL_CONFIG["num_layers"], MODEL_CONFIG["num_heads"], MODEL_CONFIG["num_kv_heads"], MODEL_CONFIG["head_dim"]
+    gk = torch.Generator(device=dev).manual_seed(MODEL_SEED + 1)
+    cache = DepthKVCache(MODEL_B, MODEL_T, 2 * N, Hk, d, device=dev, dtype=torch.bfloat16)
+    cache.k_cache.normal_(generator=gk)
+    cache.v_cache.normal_(generator=gk)
+    Kd, Vd = cache.read(MODEL_T)
+    Qa = torch.randn(MODEL_B, Hq, MODEL_T, d, device=dev, generator=gk).to(torch.bfloat16)
+    Ka = torch.randn(MODEL_B, Hk, MODEL_T, d, device=dev, generator=gk).to(torch.bfloat16)
+    Va = torch.randn(MODEL_B, Hk, MODEL_T, d, device=dev, generator=gk).to(torch.bfloat16)
+    Oa = torch.empty_like(Qa)
+    for _ in range(args.warmup):
+        moda_forward_into(Oa, Qa, Ka, Va, Kd, Vd, N, None, MODEL_CONFIG["chunk_size"])
+    torch.cuda.synchronize(dev)
+    ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ea.record(stream)
+    for _ in range(10 * args.steps):
+        moda_forward_into(Oa, Qa, Ka, Va, Kd, Vd, N, None, MODEL_CONFIG["chunk_size"])
+    eb.record(stream)
+    torch.cuda.synchronize(dev)
+    ms_layer = ea.elapsed_time(eb) / (10 * args.steps)
+    fl_layer = flops(MODEL_B, Hq, MODEL_T, d, N)
+    by_layer = hbm_bytes(MODEL_B, Hq, Hk, MODEL_T, d, N)
+    p_tflops, p_gbs, p_kind = peaks()
+    t_roof_layer = max(fl_layer / (p_tflops * 1e12), by_layer / (p_gbs * 1e9)) * 1e3
+    del cache, Kd, Vd, Qa, Ka, Va, Oa
     ms, clk = results[False]
     ms_lean, clk_lean = results[True]
     tokens = MODEL_B * MODEL_T
@@ -731,6 +761,15 @@ def run_model(args):
                                "writes: d_model=2048 H_q=16 H_k=4 d=128 24 layers FFN 8192 "
                                "B=8 T=4096", "global_batch": MODEL_B, "seq_len": MODEL_T,
                    "launch": "CUDA graph replay" if args.graph else "eager"},
+        "attention_kernel": {
+            "what": "one layer's fused attention call: B=8 H_q=16 H_k=4 T=4096 d=128 L=24, "
+                    "depth rows read through a 48-slot DepthKVCache",
+            "ms": ms_layer, "tflops": fl_layer / (ms_layer * 1e-3) / 1e12,
+            "roofline": {"bound": "tensor", "achieved": fl_layer / (ms_layer * 1e-3) / 1e12,
+                         "peak": p_tflops, "unit": "TFLOP/s",
+                         "frac": t_roof_layer / ms_layer, "peak_kind": p_kind,
+                         "roofline_ms": t_roof_layer, "algorithmic_flops": fl_layer,
+                         "algorithmic_bytes": by_layer}},
         "lean": {"value": tokens / (ms_lean * 1e-3), "unit": "tokens/s", "ms_per_step": ms_lean,
                  "max_abs_diff_vs_default": float(diff.max()),
                  "mean_abs_diff_vs_default": float(diff.mean()), "clocks": clk_lean},
@@ -815,7 +854,10 @@ def run_module(args):
                    "launch": "CUDA graph replay" if args.graph else "eager"},
         "kernel": {"ms": ms_k, "tflops": tflops, "hbm_gbs": by / (ms_k * 1e-3) / 1e9,
                    "roofline_ms": t_roof, "roofline_frac": t_roof / ms_k, "peak_kind": p_kind,
-                   "algorithmic_flops": fl, "algorithmic_bytes": by},
+                   "algorithmic_flops": fl, "algorithmic_bytes": by,
+                   "roofline": {"bound": "tensor" if fl / p_tflops >= by / p_gbs * 1e3 else "hbm",
+                                "achieved": tflops, "peak": p_tflops, "unit": "TFLOP/s",
+                                "frac": tflops / p_tflops, "peak_kind": p_kind}},
         "clocks": clk,
         "verify": {"finite": bool(torch.isfinite(O).all()), "device_status": device_status(dev)},
     }
