@@ -153,6 +153,24 @@ MODA_DEV bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
     }
 }
 
+// The same bounded wait without the back-off, for the waits on a softmax step's critical
+// path (scores ready, P ready): there the wake-up latency matters more than issue slots.
+MODA_DEV bool mbar_wait_hot(uint32_t bar, uint32_t parity, volatile int* abort_flag, int site) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 255u) == 0) {
+            if (*abort_flag) return false;
+            if (clock64() - t0 > kWaitLimitCycles) {
+                *abort_flag = 1;
+                atomicCAS(&moda_dev_status, 0, 0x100 | site);
+                return false;
+            }
+        }
+    }
+}
+
 // Bounded wait that ignores the abort flag: used only on the exit path to let
 // copies and MMAs already in flight land before shared memory / TMEM are released.
 MODA_DEV bool mbar_wait_drain(uint32_t bar, uint32_t parity) {

@@ -430,7 +430,7 @@ __global__ void __launch_bounds__(kThreads, 1) moda_fwd_tc_kernel(const __grid_c
                     const bool k_ready = ok && has_next && *issued > kf_next &&
                                          mbar_test(slot_full(kf_next % Cfg::kStages),
                                                    (kf_next / Cfg::kStages) & 1u);
-                    ok = ok && mbar_wait(p_full(x), pcnt & 1u, abort_flag, 6);
+                    ok = ok && mbar_wait_hot(p_full(x), pcnt & 1u, abort_flag, 6);
                     if (!ok) break;
                     ++pcnt;
                     if (b == 0 && items > 0) {
@@ -508,7 +508,7 @@ __global__ void __launch_bounds__(kThreads, 1) moda_fwd_tc_kernel(const __grid_c
                 const uint32_t turn_target = other_seen;
                 if (x == 0 && theirs) ++other_seen;
                 if (!mine) continue;
-                if (!mbar_wait(s_full(x), nblk & 1u, abort_flag, 8)) { ok = false; break; }
+                if (!mbar_wait_hot(s_full(x), nblk & 1u, abort_flag, 8)) { ok = false; break; }
                 tc_fence_after();
                 uint32_t sv[64];
                 {
@@ -603,13 +603,13 @@ __global__ void __launch_bounds__(kThreads, 1) moda_fwd_tc_kernel(const __grid_c
                 const float alpha = rescale ? ex2(m_run - m_use) : 1.0f;
                 m_run = m_use;
                 // wait for the other tile's turn to end (bounded; skipped after an abort)
-                // (a hint only: at most 2^20 polls, and no clock read on this hot path)
-                if (lane == 0) {
+                // (a hint only: at most 2^20 polls, and no clock read on this hot path).
+                // Every lane polls the same words, so the warp never diverges here.
+                {
                     const uint32_t need = 8u * turn_target;
                     for (uint32_t it = 0; it < (1u << 20) && *other_turns < need && !*abort_flag; ++it) {
                     }
                 }
-                __syncwarp();
                 if (__any_sync(0xffffffffu, live)) {
                     const float m_base = (m_use == -INFINITY) ? 0.f : m_use;
                     const uint64_t sc2 = f2_pack(sc, sc);
