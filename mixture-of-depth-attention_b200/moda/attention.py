@@ -43,8 +43,12 @@ class MoDAAttention(nn.Module):
                                       bias=False)
         self.use_triton = False  # kept for API parity; there is one CUDA path
         self.dropout = nn.Dropout(config.dropout) if config.dropout > 0 else nn.Identity()
-        self._w_qkv = None      # cat(W_q, W_k, W_v) for the fused projection, and the
-        self._w_qkv_key = None  # weights' (pointer, version) it was built from
+        # cat(W_q, W_k, W_v) for the fused projection (one extra copy of the three weights,
+        # (H_q + 2*H_k)*d*D elements), the weights' (pointer, version) it was built from,
+        # and whether the fused kernel takes this module's shapes (found on first use)
+        self._w_qkv = None
+        self._w_qkv_key = None
+        self._qkv_fused_ok = None
 
     def _fused_qkv_weight(self) -> Tensor:
         ws = (self.q_proj.weight, self.k_proj.weight, self.v_proj.weight)
@@ -60,11 +64,17 @@ class MoDAAttention(nn.Module):
         shape) the three nn.Linear of the reference, viewed as transposes (same values)."""
         B, T, _ = x.shape
         H_q, H_k, d = self.num_heads, self.num_kv_heads, self.head_dim
-        if not torch.is_grad_enabled() and x.is_cuda and x.dtype in (torch.bfloat16, torch.float16):
+        if (not torch.is_grad_enabled() and x.is_cuda and self._qkv_fused_ok is not False
+                and x.dtype in (torch.bfloat16, torch.float16)):
             try:
-                return qkv_proj(x.contiguous(), self._fused_qkv_weight(), H_q, H_k, d)
+                out = qkv_proj(x.contiguous(), self._fused_qkv_weight(), H_q, H_k, d)
+                self._qkv_fused_ok = True
+                return out
             except MoDAUnsupported:
-                pass
+                # refused on the host before any launch (e.g. d not a multiple of 32): use
+                # the library GEMMs for this module from now on
+                self._qkv_fused_ok = False
+                self._w_qkv = None
         # [B, H, T, d] views with strides (T*H*d, d, H*d, 1): the kernel reads them in place
         Q = self.q_proj(x).view(B, T, H_q, d).transpose(1, 2)
         K = self.k_proj(x).view(B, T, H_k, d).transpose(1, 2)

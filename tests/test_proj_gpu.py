@@ -148,3 +148,21 @@ def test_module_uses_fused_qkv_without_autograd():
         assert (fast.float() - ref.float()).abs().max().item() <= TOL
         with torch.no_grad():
             attn.k_proj.weight.mul_(0.5)  # bumps the version: the fused weight is rebuilt
+
+
+def test_module_falls_back_to_library_gemms_for_shapes_the_fused_kernel_refuses():
+    """head_dim 16 (not a multiple of 32): the fused Q/K/V kernel refuses on the host, the
+    module remembers it and uses the three nn.Linear; output as with autograd."""
+    from moda import MoDAAttention, MoDAConfig
+    torch.manual_seed(1)
+    cfg = MoDAConfig(d_model=64, num_heads=4, num_kv_heads=2, head_dim=16, num_layers=2)
+    attn = MoDAAttention(cfg).cuda().to(torch.bfloat16)
+    x = torch.randn(1, 40, 64, device="cuda", dtype=torch.bfloat16)
+    Kd = torch.randn(1, 2, 80, 16, device="cuda", dtype=torch.bfloat16)
+    Vd = torch.randn_like(Kd)
+    for _ in range(2):
+        with torch.no_grad():
+            fast = attn(x, Kd, Vd)[0]
+        assert attn._qkv_fused_ok is False
+    ref = attn(x, Kd, Vd)[0].detach()
+    assert (fast.float() - ref.float()).abs().max().item() <= TOL
