@@ -11,9 +11,9 @@
 //     tile is used once by all G heads of its group -- GQA without
 //     repeat_interleave.
 //   * A work item is a pair of consecutive query tiles (A, B) of one (b, KV head).
-//     The kernel is persistent: one CTA per SM walks the items heaviest first
-//     (most causal blocks first) with a fixed stride, so the producer already
-//     streams the next item while the current one drains.
+//     The kernel is persistent: one CTA per SM walks the items, sorted heaviest
+//     first (most causal blocks first), in serpentine rounds (see round_item), so
+//     the producer already streams the next item while the current one drains.
 //   * Each item walks one list of 128-row key blocks shared by both tiles:
 //       - causal sequence blocks j = 0..S-1 (keys [128j, 128j+128)), masked on the
 //         diagonal; both tiles read the same K/V fill;
@@ -204,6 +204,15 @@ __global__ void __launch_bounds__(kThreads, 1) moda_fwd_tc_kernel(const __grid_c
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    // Items in serpentine order: round r hands the CTAs items [r*grid, (r+1)*grid) in
+    // CTA order for even r and in reverse for odd r. Items are sorted heaviest first, so
+    // a fixed stride would give CTA 0 the heaviest item of every round; alternating the
+    // direction pairs a heavier item with a lighter one. Every role of the CTA walks the
+    // same sequence.
+    auto round_item = [&](int round) {
+        const int g = static_cast<int>(gridDim.x);
+        return round * g + ((round & 1) ? g - 1 - static_cast<int>(blockIdx.x) : static_cast<int>(blockIdx.x));
+    };
 
     if (threadIdx.x == 0) {
         for (int x = 0; x < 2; ++x) {
@@ -254,7 +263,7 @@ __global__ void __launch_bounds__(kThreads, 1) moda_fwd_tc_kernel(const __grid_c
             // the next release to wait for from each tile (1 bit per slot)
             uint32_t cons = 0, par_a = 0, par_b = 0;
             bool ok = true;
-            for (int item = blockIdx.x; item < p.num_items && ok; item += gridDim.x) {
+            for (int round = 0, item = round_item(0); item < p.num_items && ok; item = round_item(++round)) {
                 const Item it = item_info(p, item);
 #pragma unroll
                 for (int x = 0; x < 2; ++x) {
@@ -378,7 +387,7 @@ __global__ void __launch_bounds__(kThreads, 1) moda_fwd_tc_kernel(const __grid_c
             uint32_t pcnt = 0;    // P blocks consumed
             uint32_t items = 0;   // items of this tile started
             bool ok = true;
-            for (int item = blockIdx.x; item < p.num_items && ok; item += gridDim.x) {
+            for (int round = 0, item = round_item(0); item < p.num_items && ok; item = round_item(++round)) {
                 const Item it = item_info(p, item);
                 const TileInfo ti = x == 0 ? it.t[0] : it.t[1];
                 if (ti.len() == 0) {
@@ -486,7 +495,7 @@ __global__ void __launch_bounds__(kThreads, 1) moda_fwd_tc_kernel(const __grid_c
         uint32_t other_before = 0;  // blocks of the other tile in earlier items
         volatile uint32_t* other_turns = exp_turns + (x ^ 1);
         bool ok = true;
-        for (int item = blockIdx.x; item < p.num_items && ok; item += gridDim.x) {
+        for (int round = 0, item = round_item(0); item < p.num_items && ok; item = round_item(++round)) {
             const Item it = item_info(p, item);
             const TileInfo ti = x == 0 ? it.t[0] : it.t[1];
             const int other_len = x == 0 ? it.t[1].len() : it.t[0].len();

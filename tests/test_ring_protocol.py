@@ -45,6 +45,25 @@ def item_steps(tA, tB):
     return out
 
 
+def serpentine_items(cta, items, grid):
+    """The kernel's item order for one CTA: round r covers items [r*grid, (r+1)*grid), in
+    CTA order for even r and reversed for odd r; the walk stops at the first item out of
+    range."""
+    r = 0
+    while True:
+        item = r * grid + (grid - 1 - cta if r & 1 else cta)
+        if item >= items:
+            return
+        yield item
+        r += 1
+
+
+def test_serpentine_order_covers_every_item_once():
+    for items, grid in ((512, 148), (4096, 148), (100, 148), (1, 1), (37, 5)):
+        seen = sorted(i for c in range(min(grid, items)) for i in serpentine_items(c, items, min(grid, items)))
+        assert seen == list(range(items))
+
+
 def build_schedule(B, Hk, T, L, G, grid):
     """Fill list (readers per fill) and per-issuer programs for CTA 0..grid-1."""
     n_tok = 128 // G
@@ -56,7 +75,7 @@ def build_schedule(B, Hk, T, L, G, grid):
         fills = []                       # readers bitmask per fill
         progs = ([], [])                 # per tile: list of ('full', f) / ('p', blk) / ('rel', f)
         blk = [0, 0]
-        for item in range(cta, items, grid):
+        for item in serpentine_items(cta, items, min(grid, items)):
             pair = num_pairs - 1 - item // (B * Hk)
             tiles = [tile_info(T, L, n_tok, pair, x) for x in (0, 1)]
             blocks = [[], []]            # per tile: (kfill, vfill)
