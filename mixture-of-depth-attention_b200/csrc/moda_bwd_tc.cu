@@ -132,6 +132,13 @@ __global__ void __launch_bounds__(kBThreads, 1) moda_bwd_tc_kernel(const __grid_
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Cfg::kMiscOff + 8);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr uint32_t kTile = Cfg::kTile;
+    // Items (sorted heaviest first) in serpentine rounds: round r hands the CTAs items
+    // [r*grid, (r+1)*grid) in CTA order for even r and in reverse for odd r, so no CTA
+    // gets the heaviest item of every round. Every role walks the same sequence.
+    auto round_item = [&](int round) {
+        const int g = static_cast<int>(gridDim.x);
+        return round * g + ((round & 1) ? g - 1 - static_cast<int>(blockIdx.x) : static_cast<int>(blockIdx.x));
+    };
 
     if (threadIdx.x == 0) {
         mbar_init(res_full, 1);
@@ -184,7 +191,7 @@ __global__ void __launch_bounds__(kBThreads, 1) moda_bwd_tc_kernel(const __grid_
                     }
                 }
             };
-            for (int item = blockIdx.x; item < p.num_items && ok; item += gridDim.x) {
+            for (int round = 0, item = round_item(0); item < p.num_items && ok; item = round_item(++round)) {
                 const BwdItem it = bwd_item<MODE>(p, item);
                 ok = bwait(res_empty, (nres & 1u) ^ 1u, abort_flag, 1);
                 if (!ok) break;
@@ -263,7 +270,7 @@ __global__ void __launch_bounds__(kBThreads, 1) moda_bwd_tc_kernel(const __grid_
                                desc_join(v0 + (((4 * h + kk) * 2048) >> 4), hi), idesc_o, (first && kk == 0) ? 0u : 1u);
                 }
             };
-            for (int item = blockIdx.x; item < p.num_items && ok; item += gridDim.x) {
+            for (int round = 0, item = round_item(0); item < p.num_items && ok; item = round_item(++round)) {
                 const BwdItem it = bwd_item<MODE>(p, item);
                 ok = bwait(res_full, nres & 1u, abort_flag, 3);
                 if (!ok) break;
@@ -324,7 +331,7 @@ __global__ void __launch_bounds__(kBThreads, 1) moda_bwd_tc_kernel(const __grid_
         const int gsh = __ffs(p.G) - 1;  // G divides 128: a power of two
         uint32_t nst = 0, nitems = 0;
         bool ok = true;
-        for (int item = blockIdx.x; item < p.num_items && ok; item += gridDim.x) {
+        for (int round = 0, item = round_item(0); item < p.num_items && ok; item = round_item(++round)) {
             const BwdItem it = bwd_item<MODE>(p, item);
             // DQ: this thread's query row; its lse and D stay in registers
             int tok_r = 0;
