@@ -107,6 +107,8 @@ def _moda_chunked(Q, K, V, Kd, Vd, L, scale, C):
 
 
 def _softmax(s):
+    if s.size == 0:  # torch.softmax of an empty tensor is that empty tensor (T = 0 or B = 0)
+        return s.copy()
     m = np.max(s, axis=-1, keepdims=True)
     e = np.exp(s - m)
     return e / np.sum(e, axis=-1, keepdims=True)
@@ -223,10 +225,15 @@ def moda_attention_grads(Q, K, V, K_depth, V_depth, num_layers, dO, scale=None,
     keep_dep = (np.arange(T * L) // L)[None, :] == np.arange(T)[:, None]
     keep = np.concatenate([keep_seq, keep_dep], axis=1)
     s = np.where(keep[None, None], s, -np.inf)
-    m = np.max(s, axis=-1, keepdims=True)
-    e = np.exp(s - m)
-    l = np.sum(e, axis=-1, keepdims=True)
-    P = e / l
+    if s.shape[-1] == 0:  # T = 0: no rows, no keys; torch's autograd returns empty gradients
+        m = np.zeros(s.shape[:-1] + (1,), dtype)
+        l = np.ones_like(m)
+        P = s.copy()
+    else:
+        m = np.max(s, axis=-1, keepdims=True)
+        e = np.exp(s - m)
+        l = np.sum(e, axis=-1, keepdims=True)
+        P = e / l
     O = np.matmul(P, Ve)
     dP = np.matmul(dO, np.swapaxes(Ve, -1, -2))
     dS = P * (dP - np.sum(dO * O, axis=-1, keepdims=True))

@@ -109,6 +109,22 @@ def test_autograd_through_moda_attention_cuda():
         assert rel_err(host(t.grad), ref[k]) <= FP32_REL_TOL, k
 
 
+@pytest.mark.parametrize("shape", [(2, 4, 2, 0, 64, 3), (0, 4, 2, 5, 128, 3)], ids=["T0", "B0"])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16], ids=["fp32", "bf16"])
+def test_autograd_on_empty_inputs(shape, dtype):
+    """Empty sequence or batch: the reference's autograd gives empty gradients of the
+    inputs' shapes (oracle too); so does the CUDA backward."""
+    B, H_q, H_k, T, d, L = shape
+    arrs = seeded_inputs(B, H_q, H_k, T, d, L, seed=53)
+    ins = [t.requires_grad_(True) for t in dev(arrs, dtype)]
+    out = moda_attention_cuda(*ins, num_layers=L)
+    out.sum().backward()
+    torch.cuda.synchronize()
+    ref = orc.moda_attention_grads(*arrs, L, np.ones((B, H_q, T, d)))
+    for t, k in zip(ins, GRADS):
+        assert t.grad is not None and tuple(t.grad.shape) == ref[k].shape == tuple(t.shape), k
+
+
 def test_autograd_matches_direct_backward_with_strided_views():
     """MoDAAttention hands the kernel transposed views; gradients flow back into them."""
     B, Hq, Hk, T, d, L = 2, 4, 2, 24, 64, 3

@@ -98,6 +98,22 @@ SHAPES = [
 ]
 
 
+EMPTY = [(2, 4, 2, 0, 128, 3), (0, 4, 2, 5, 128, 3), (2, 8, 2, 0, 64, 32)]
+
+
+@pytest.mark.parametrize("shape", EMPTY, ids=[str(s) for s in EMPTY])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16], ids=["fp32", "bf16"])
+@pytest.mark.parametrize("chunk", [None, 4])
+def test_empty_inputs_give_empty_output(shape, dtype, chunk):
+    """The reference returns an empty O of Q's shape for T = 0 or B = 0 (oracle too)."""
+    B, Hq, Hk, T, d, L = shape
+    arrs = seeded_inputs(B, Hq, Hk, T, d, L, seed=11)
+    out = moda_attention_cuda(*dev(arrs, dtype), L, None, chunk)
+    torch.cuda.synchronize()
+    ref = orc.moda_attention_naive(*arrs, L, chunk_size=chunk)
+    assert tuple(out.shape) == ref.shape == (B, Hq, T, d) and out.dtype == dtype
+
+
 @pytest.mark.parametrize("shape", SHAPES, ids=[str(s) for s in SHAPES])
 def test_tc_matches_oracle_bf16(shape):
     B, Hq, Hk, T, d, L = shape

@@ -70,6 +70,20 @@ def test_oracle_depth_rows_short_raises():
         orc.moda_attention_naive(Q, K, V, Kd[:, :, :20], Vd[:, :, :20], 3, chunk_size=4)
 
 
+@pytest.mark.parametrize("shape", [(2, 4, 2, 0, 32, 3), (0, 4, 2, 5, 32, 3)], ids=["T0", "B0"])
+@pytest.mark.parametrize("chunk", [None, 4])
+def test_oracle_empty_inputs(shape, chunk):
+    # moda_attention_naive on an empty sequence (T = 0) or batch (B = 0) returns an empty
+    # O of Q's shape (torch's matmul / softmax of empty tensors), and autograd gives empty
+    # gradients of the inputs' shapes; the oracle does the same.
+    B, Hq, Hk, T, d, L = shape
+    arrs = seeded_inputs(B, Hq, Hk, T, d, L, seed=10)
+    assert orc.moda_attention_naive(*arrs, L, chunk_size=chunk).shape == (B, Hq, T, d)
+    g = orc.moda_attention_grads(*arrs, L, np.zeros((B, Hq, T, d)))
+    for k, a in zip(("dQ", "dK", "dV", "dK_depth", "dV_depth"), arrs):
+        assert g[k].shape == a.shape, k
+
+
 def test_oracle_causal_and_depth_isolation():
     # reference tests/test_kernel.py:32-59, restated on the oracle
     Q, K, V, Kd, Vd = seeded_inputs(1, 1, 1, 4, 8, 3, seed=9)
