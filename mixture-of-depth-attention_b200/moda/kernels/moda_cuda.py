@@ -16,6 +16,7 @@ from typing import Optional
 
 import torch
 from torch import Tensor
+from torch.autograd.function import once_differentiable
 
 from . import _lib
 
@@ -141,7 +142,10 @@ def moda_backward(dO: Tensor, Q: Tensor, K: Tensor, V: Tensor, K_depth: Tensor,
 
 class _MoDAFunction(torch.autograd.Function):
     """Forward and backward both run in libmoda_b200.so: the forward saves O and the
-    row log-sum-exp; the backward kernels recompute the attention weights from them."""
+    row log-sum-exp; the backward kernels recompute the attention weights from them.
+    First derivatives only: differentiating the gradients (double backward, which torch
+    autograd gives the reference's moda_attention_naive) raises instead of returning
+    gradients that ignore the backward's own dependence on the inputs."""
 
     @staticmethod
     def forward(ctx, Q, K, V, K_depth, V_depth, num_layers, scale, chunk_size, kernel):
@@ -153,6 +157,7 @@ class _MoDAFunction(torch.autograd.Function):
         return O
 
     @staticmethod
+    @once_differentiable
     def backward(ctx, dO):
         Q, K, V, Kd, Vd, O, lse = ctx.saved_tensors
         grads = moda_backward(dO, Q, K, V, Kd, Vd, O, lse, ctx.num_layers, ctx.scale)
@@ -236,6 +241,7 @@ class _ZeroDepthFunction(torch.autograd.Function):
         return O
 
     @staticmethod
+    @once_differentiable
     def backward(ctx, dO):
         Q, K, V, O, lse = ctx.saved_tensors
         empty = Q.new_empty(Q.shape[0], K.shape[1], 0, Q.shape[3])

@@ -125,6 +125,19 @@ def test_autograd_on_empty_inputs(shape, dtype):
         assert t.grad is not None and tuple(t.grad.shape) == ref[k].shape == tuple(t.shape), k
 
 
+def test_double_backward_raises():
+    """Second derivatives are not implemented: differentiating a gradient of the CUDA
+    attention raises (the backward is once-differentiable) rather than returning values
+    that miss the backward's dependence on its inputs."""
+    B, H, T, L, d = 1, 2, 6, 2, 16
+    arrs = seeded_inputs(B, H, H, T, d, L, seed=54)
+    ins = [t.requires_grad_(True) for t in dev(arrs, torch.float32)]
+    out = moda_attention_cuda(*ins, num_layers=L)
+    (gq,) = torch.autograd.grad(out.square().sum(), ins[0], create_graph=True)
+    with pytest.raises(RuntimeError):
+        gq.sum().backward()
+
+
 def test_autograd_matches_direct_backward_with_strided_views():
     """MoDAAttention hands the kernel transposed views; gradients flow back into them."""
     B, Hq, Hk, T, d, L = 2, 4, 2, 24, 64, 3
