@@ -39,6 +39,12 @@ class MoDAUnsupported(RuntimeError):
     host before any launch)."""
 
 
+class MoDADtypeError(TypeError, RuntimeError):
+    """Unsupported or mixed dtypes. A TypeError, and also a RuntimeError like the one
+    torch raises inside moda_attention_naive for mixed dtypes ("expected scalar type ...");
+    float64, which the reference computes in, has no kernel here."""
+
+
 class MoDAShapeError(ValueError, RuntimeError):
     """Inconsistent shapes. A ValueError, and also a RuntimeError like the shape
     errors moda_attention_naive raises for the same inputs (moda_naive.py:137-149)."""
@@ -115,7 +121,7 @@ def check(code: int, what: str) -> None:
     if code == MODA_ERR_ARG:
         raise ValueError(msg)
     if code == MODA_ERR_DTYPE:
-        raise TypeError(msg)
+        raise MoDADtypeError(msg)
     if code == MODA_ERR_UNSUPPORTED:
         raise MoDAUnsupported(msg)
     raise RuntimeError(msg)

@@ -42,13 +42,13 @@ def _check_inputs(Q, K, V, K_depth, V_depth):
                 f"moda_attention_cuda runs on CUDA tensors only ({n} is on {t.device}); "
                 "there is no CPU path")
         if t.dtype not in _DTYPES:
-            raise TypeError(f"{n} has unsupported dtype {t.dtype} (float32, bfloat16, float16)")
+            raise _lib.MoDADtypeError(f"{n} has unsupported dtype {t.dtype} (float32, bfloat16, float16)")
     dev, dt = Q.device, Q.dtype
     for n, t in zip(names, ts):
         if t.device != dev:
             raise RuntimeError(f"{n} is on {t.device}, Q on {dev}")
         if t.dtype != dt:
-            raise TypeError(f"{n} has dtype {t.dtype}, Q has {dt}")
+            raise _lib.MoDADtypeError(f"{n} has dtype {t.dtype}, Q has {dt}")
 
 
 def _check_out(out: Tensor, Q: Tensor) -> Tensor:
@@ -78,6 +78,8 @@ def moda_forward_into(O: Tensor, Q: Tensor, K: Tensor, V: Tensor, K_depth: Tenso
 
 def moda_plan(Q, K, V, K_depth, V_depth, num_layers: int, kernel: str = "auto") -> str:
     """Which kernel a call would launch ("tc" or "simt"). Host-only; works on any device."""
+    if Q.dtype not in _DTYPES:
+        raise _lib.MoDADtypeError(f"Q has unsupported dtype {Q.dtype} (float32, bfloat16, float16)")
     O_shape = (Q.shape[0], Q.shape[1], Q.shape[2], Q.shape[3])
     o = _lib.describe(Q.data_ptr(), O_shape, Q.stride())
     code = _lib.load().moda_fwd_plan(_desc(Q), _desc(K), _desc(V), _desc(K_depth),
@@ -276,11 +278,11 @@ def depth_append(k_cache: Tensor, v_cache: Tensor, layer_idx: int, k: Tensor, v:
         if t.dim() != 4:
             raise _lib.MoDAShapeError(f"{n} must be 4-D")
         if t.dtype != k_cache.dtype:
-            raise TypeError(f"{n} has dtype {t.dtype}, cache has {k_cache.dtype}")
+            raise _lib.MoDADtypeError(f"{n} has dtype {t.dtype}, cache has {k_cache.dtype}")
         if t.device != k_cache.device:
             raise RuntimeError(f"{n} is on {t.device}, cache on {k_cache.device}")
     if k_cache.dtype not in _DTYPES:
-        raise TypeError(f"unsupported cache dtype {k_cache.dtype}")
+        raise _lib.MoDADtypeError(f"unsupported cache dtype {k_cache.dtype}")
     lib = _lib.load()
     stream = torch.cuda.current_stream(k_cache.device).cuda_stream
     with torch.cuda.device(k_cache.device):
@@ -305,11 +307,11 @@ def depth_proj_append(x: Tensor, w_kv: Tensor, k_cache: Tensor, v_cache: Tensor,
         if t.device != x.device:
             raise RuntimeError(f"{n} is on {t.device}, x on {x.device}")
         if t.dtype != x.dtype:
-            raise TypeError(f"{n} has dtype {t.dtype}, x has {x.dtype}")
+            raise _lib.MoDADtypeError(f"{n} has dtype {t.dtype}, x has {x.dtype}")
     if x.dim() != 3 or w_kv.dim() != 2:
         raise _lib.MoDAShapeError("x must be [B, T, D] and w_kv [2*H_k*d, D]")
     if x.dtype not in _DTYPES:
-        raise TypeError(f"unsupported dtype {x.dtype}")
+        raise _lib.MoDADtypeError(f"unsupported dtype {x.dtype}")
     lib = _lib.load()
     stream = torch.cuda.current_stream(x.device).cuda_stream
     with torch.cuda.device(x.device):
@@ -336,11 +338,11 @@ def qkv_proj(x: Tensor, w_qkv: Tensor, num_heads: int, num_kv_heads: int,
         if t.device != x.device:
             raise RuntimeError(f"{n} is on {t.device}, x on {x.device}")
         if t.dtype != x.dtype:
-            raise TypeError(f"{n} has dtype {t.dtype}, x has {x.dtype}")
+            raise _lib.MoDADtypeError(f"{n} has dtype {t.dtype}, x has {x.dtype}")
     if x.dim() != 3 or w_qkv.dim() != 2:
         raise _lib.MoDAShapeError("x must be [B, T, D] and w_qkv [(H_q+2*H_k)*d, D]")
     if x.dtype not in _DTYPES:
-        raise TypeError(f"unsupported dtype {x.dtype}")
+        raise _lib.MoDADtypeError(f"unsupported dtype {x.dtype}")
     B, T, _ = x.shape
     Q = x.new_empty(B, num_heads, T, head_dim)
     K = x.new_empty(B, num_kv_heads, T, head_dim)

@@ -102,6 +102,22 @@ def test_shape_mismatches_raise(bad):
                   _t((B, Hk, T * L, d)), L)
 
 
+def test_dtype_errors_are_type_and_runtime_errors():
+    # torch raises RuntimeError inside moda_attention_naive for mixed dtypes; the drop-in's
+    # dtype errors are both TypeError and RuntimeError, from the host checks and from the
+    # C ABI's status code alike
+    x = _t((1, 2, 8, 64))
+    x64 = torch.zeros(1, 2, 8, 64, dtype=torch.float64)
+    with pytest.raises(TypeError):
+        moda_plan(x64, x64, x64, x64, x64, 1)
+    with pytest.raises(RuntimeError):
+        moda_plan(x64, x64, x64, x64, x64, 1)
+    with pytest.raises(_lib.MoDADtypeError):
+        _lib.check(_lib.MODA_ERR_DTYPE, "moda_fwd")
+    assert issubclass(_lib.MoDADtypeError, TypeError) and issubclass(_lib.MoDADtypeError, RuntimeError)
+    assert moda_plan(x, x, x, x, x, 1) in ("tc", "simt")
+
+
 def test_negative_num_layers_rejected():
     x = _t((1, 2, 8, 64))
     with pytest.raises(ValueError):
