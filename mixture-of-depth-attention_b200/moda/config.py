@@ -1,4 +1,9 @@
-"""MoDA configuration (field-for-field the reference's moda/config.py:7-60)."""
+"""MoDAConfig: the hyper-parameters the MoDA modules read.
+
+The fields, their order, defaults and derived values are the reference's
+(moda/config.py:7-60), so a config written for the reference builds the same model
+here; only ``lean_depth_cache`` is added, off by default.
+"""
 
 from dataclasses import dataclass
 from typing import Optional
@@ -6,25 +11,26 @@ from typing import Optional
 
 @dataclass
 class MoDAConfig:
-    """Configuration for MoDA (Mixture-of-Depths Attention).
+    """Hyper-parameters of a MoDA transformer.
 
-    Attributes:
-        d_model: Model dimension (D).
-        num_heads: Number of query attention heads (H_q).
-        num_kv_heads: Number of KV attention heads (H_k). Defaults to num_heads.
-        head_dim: Per-head dimension (d). Defaults to d_model // num_heads.
-        num_layers: Number of transformer layers; also the L that MoDAAttention
-            passes to the kernel (moda/attention.py:90).
-        chunk_size: Query chunk size (C). Kept for API parity; the fused kernel
-            is chunk-aware by construction (a tile of n tokens reads n*L depth
-            rows) and its result does not depend on C.
-        ffn_dim: FFN intermediate dimension. Defaults to 4 * d_model.
-        dropout: Attention dropout probability.
-        max_seq_len: Maximum sequence length.
-        use_triton: Accepted for API parity and ignored: CUDA tensors always run
-            the B200 kernel.
-        post_norm: Use post-norm (True) vs pre-norm (False).
-        lean_depth_cache: Opt-in (not in the reference; default False keeps its
+    Fields:
+        d_model: width of the residual stream.
+        num_heads: query heads, H_q.
+        num_kv_heads: key/value heads, H_k; None means H_q (every query head has
+            its own K/V head).
+        head_dim: width of one head, d; None means d_model // num_heads.
+        num_layers: transformer blocks. The attention also uses it as L, the
+            number of depth rows per token it reads (moda/attention.py:90).
+        chunk_size: the reference's query chunk C for its depth kernel. Accepted;
+            the fused kernel reads only the n*L depth rows of an n-token tile by
+            construction, and its result does not depend on C.
+        ffn_dim: feed-forward width; None means 4 * d_model.
+        dropout: attention dropout probability.
+        max_seq_len: longest sequence the model is built for.
+        use_triton: accepted and ignored: CUDA tensors always run the B200 kernel.
+        post_norm: normalise after each residual add (True) or before each
+            sublayer (False).
+        lean_depth_cache: opt-in, not in the reference (False keeps its
             behaviour). MoDAModel then skips the depth-cache work whose result no
             layer reads: the zero-fill of cache rows the attention never addresses,
             writes into those rows and their projections, the last layer's writes,
@@ -47,23 +53,25 @@ class MoDAConfig:
     lean_depth_cache: bool = False
 
     def __post_init__(self):
+        # fill the derived defaults, then require whole KV groups (the reference
+        # asserts the same condition, so the error type is AssertionError too)
         if self.num_kv_heads is None:
             self.num_kv_heads = self.num_heads
         if self.head_dim is None:
             self.head_dim = self.d_model // self.num_heads
         if self.ffn_dim is None:
             self.ffn_dim = 4 * self.d_model
-        assert self.num_heads % self.num_kv_heads == 0, (
-            f"num_heads ({self.num_heads}) must be divisible by "
-            f"num_kv_heads ({self.num_kv_heads})"
-        )
+        if self.num_heads % self.num_kv_heads != 0:
+            raise AssertionError(
+                f"{self.num_heads} query heads cannot be split into groups over "
+                f"{self.num_kv_heads} key/value heads")
 
     @property
     def gqa_groups(self) -> int:
-        """Number of query heads per KV head (G)."""
+        """G: how many query heads share one key/value head."""
         return self.num_heads // self.num_kv_heads
 
     @property
     def kv_dim(self) -> int:
-        """Total KV dimension: num_kv_heads * head_dim."""
+        """Width of the key (or value) projection output: H_k * d."""
         return self.num_kv_heads * self.head_dim
