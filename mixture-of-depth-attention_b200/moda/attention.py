@@ -19,7 +19,7 @@ from .kernels.moda_cuda import moda_attention_cuda, moda_attention_zero_depth, q
 
 
 class MoDAAttention(nn.Module):
-    """Mixture-of-Depths Attention.
+    """MoDA attention layer (the reference's module API, moda/attention.py:16-116).
 
     Attends to the causal sequence KV of this layer and to the depth KV that
     preceding layers wrote for the same token, in one softmax.

@@ -63,10 +63,10 @@ class DepthKVCache:
         """Write layer ``layer_idx``'s depth KV: row t*L + layer_idx <- token t.
 
         Args:
-            layer_idx: Which layer is writing (0 to num_layers-1).
+            layer_idx: the writing layer's slot, 0 <= layer_idx < num_layers.
             k_depth: [B, H_k, T, d] depth keys (any strides).
             v_depth: [B, H_k, T, d] depth values.
-            seq_len: Sequence length (defaults to k_depth.shape[2]).
+            seq_len: tokens to write; None writes all k_depth.shape[2] of them.
         """
         T = seq_len or k_depth.shape[2]
         self._seq_len = max(self._seq_len, T)
