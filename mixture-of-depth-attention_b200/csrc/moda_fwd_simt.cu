@@ -114,7 +114,308 @@ __global__ void __launch_bounds__(kSimtRows * 32)
     }
 }
 
+// ---------------------------------------------------------------- fp32, tiled
+// The fp32 forward on CUDA cores, tiled like a GEMM so that every value read from
+// shared memory feeds several FMAs (the warp-per-row kernel above re-reads each key for
+// every query row and reduces every dot product across a warp). fp32 FMA throughout, so
+// the fp32 tolerance holds; only the summation order differs from the row kernel.
+//
+// A CTA (512 threads) takes 128 consecutive tokens of one query head. Thread (ty, tx),
+// ty = tid / 16, tx = tid % 16, owns query rows ty + 32i (i < 4) and, of each 64-key
+// tile, keys tx + 16j (j < 4); of the output it owns columns [tx*OC, tx*OC + OC),
+// OC = HD / 16. The 16 threads of a row sit in one half-warp, so row maxima and sums are
+// 4 shuffles. Per CTA:
+//   1. the depth rows first: for each of its rows, the row's 16 threads take L depth rows
+//      (two per thread per 32-row chunk), compute their scores against Q from shared
+//      memory, softmax them, and accumulate P.V_depth straight into their own O columns;
+//      this seeds the online softmax (m, l, O);
+//   2. the causal keys in 64-key tiles: S = Q K^T from shared memory (4 x 4 per thread),
+//      the diagonal tiles masked, online softmax, P through shared memory, O += P V.
+//      K and V tiles arrive by cp.async; the next tile's K is copied during the softmax
+//      and P.V of this one, the next V during the next S.
+// Shared memory rows are padded by 4 floats, so the 16 rows a half-warp reads at one
+// column fall into different banks.
+constexpr int kF32Rows = 128, kF32Keys = 64, kF32Threads = 512;
+
+template <int HD>
+struct F32Cfg {
+    static constexpr int kStride = HD + 4;                     // floats per staged row
+    static constexpr int kQ = 0;                                // Q   [128][HD+4]
+    static constexpr int kK = kQ + kF32Rows * kStride;          // K   [64][HD+4]
+    static constexpr int kV = kK + kF32Keys * kStride;          // V   [64][HD+4]
+    static constexpr int kP = kV + kF32Keys * kStride;          // P   [128][64+4]
+    static constexpr int kFloats = kP + kF32Rows * (kF32Keys + 4);
+    static constexpr int kBytes = kFloats * 4;
+};
+
+// 16-byte cp.async; src_bytes 0 writes zeros and reads nothing
+MODA_DEV void f32_cp16(float* dst, const float* src, int src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
+                 "r"(src_bytes)
+                 : "memory");
+}
+MODA_DEV void f32_cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+MODA_DEV void f32_cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+template <int HD>
+__global__ void __launch_bounds__(kF32Threads, 1) moda_fwd_f32_tiled_kernel(const FwdParams p) {
+    using C = F32Cfg<HD>;
+    constexpr int OC = HD / 16;
+    extern __shared__ __align__(16) float f32_smem[];
+    float* sQ = f32_smem + C::kQ;
+    float* sK = f32_smem + C::kK;
+    float* sV = f32_smem + C::kV;
+    float* sP = f32_smem + C::kP;
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    const int ntiles = (p.T + kF32Rows - 1) / kF32Rows;
+    const int t0 = (ntiles - 1 - static_cast<int>(blockIdx.x)) * kF32Rows;  // heaviest first
+    const int h = blockIdx.y, b = blockIdx.z, hk = h / p.G;
+    const int d = p.d;
+    const float* qb = static_cast<const float*>(p.q.ptr) + b * p.q.strides[0] + h * p.q.strides[1];
+    const float* kb = static_cast<const float*>(p.k.ptr) + b * p.k.strides[0] + hk * p.k.strides[1];
+    const float* vb = static_cast<const float*>(p.v.ptr) + b * p.v.strides[0] + hk * p.v.strides[1];
+    const float sc = p.scale * kLog2e;
+
+    // stage `rows` rows starting at row0 of a [.., rows, d] view into dst (zeros past T or d)
+    auto stage = [&](float* dst, const float* base, int64_t rstride, int row0, int rows, int limit) {
+        for (int i = tid; i < rows * (HD / 4); i += kF32Threads) {
+            const int r = i / (HD / 4), c4 = i % (HD / 4);
+            const bool ok = row0 + r < limit && 4 * c4 < d;
+            const float* src = ok ? base + static_cast<int64_t>(row0 + r) * rstride + 4 * c4 : base;
+            f32_cp16(dst + r * C::kStride + 4 * c4, src, ok ? 16 : 0);
+        }
+    };
+    const int kmax = min(t0 + kF32Rows, p.T);           // keys [0, kmax) are needed
+    const int nkt = (kmax + kF32Keys - 1) / kF32Keys;    // causal key tiles
+    stage(sQ, qb, p.q.strides[2], t0, kF32Rows, p.T);
+    f32_cp_commit();
+    stage(sK, kb, p.k.strides[2], 0, kF32Keys, p.T);
+    f32_cp_commit();
+    stage(sV, vb, p.v.strides[2], 0, kF32Keys, p.T);
+    f32_cp_commit();
+
+    float o[4][OC], m[4], l[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        m[i] = -INFINITY;
+        l[i] = 0.f;
+#pragma unroll
+        for (int c = 0; c < OC; ++c) o[i][c] = 0.f;
+    }
+    f32_cp_wait<2>();  // Q
+    __syncthreads();
+
+    // ---- 1. depth rows: row ty + 32i is token t0 + ty + 32i; its 16 threads split the L rows
+    if (p.L > 0) {
+        const float* kdb = static_cast<const float*>(p.kd.ptr) + b * p.kd.strides[0] + hk * p.kd.strides[1];
+        const float* vdb = static_cast<const float*>(p.vd.ptr) + b * p.vd.strides[0] + hk * p.vd.strides[1];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {  // unrolled: o, m and l stay in registers
+            const int r = ty + 32 * i, t = t0 + r;
+            // rows past T (last tile) run the same shuffles with nothing read or kept: the
+            // two rows of a warp must stay converged
+            const bool valid = t < p.T;
+            const float* qr = sQ + r * C::kStride;
+            const int64_t row0 = static_cast<int64_t>(valid ? t : 0) * p.L;
+#pragma unroll 1
+            for (int l0 = 0; l0 < p.L; l0 += 32) {
+                float s2[2];
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const int li = l0 + tx + 16 * e;
+                    s2[e] = -INFINITY;
+                    if (valid && li < p.L) {
+                        const float* kr = kdb + (row0 + li) * p.kd.strides[2];
+                        float acc = 0.f;
+                        for (int c = 0; c < d; c += 4) {
+                            const float4 kv = *reinterpret_cast<const float4*>(kr + c);
+                            const float4 qv = *reinterpret_cast<const float4*>(qr + c);
+                            acc = fmaf(qv.x, kv.x, acc);
+                            acc = fmaf(qv.y, kv.y, acc);
+                            acc = fmaf(qv.z, kv.z, acc);
+                            acc = fmaf(qv.w, kv.w, acc);
+                        }
+                        s2[e] = acc * sc;
+                    }
+                }
+                float mx = fmaxf(s2[0], s2[1]);
+#pragma unroll
+                for (int off = 1; off < 16; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+                // finite for a valid row: the chunk has >= 1 depth row
+                const float m_new = valid ? fmaxf(m[i], mx) : 0.f;
+                const float alpha = valid ? ex2(m[i] - m_new) : 1.f;
+                const float p0 = valid ? ex2(s2[0] - m_new) : 0.f, p1 = valid ? ex2(s2[1] - m_new) : 0.f;
+                l[i] = fmaf(l[i], alpha, p0 + p1);  // this thread's share of the row sum
+                if (valid) m[i] = m_new;
+#pragma unroll
+                for (int c = 0; c < OC; ++c) o[i][c] *= alpha;
+                const int nrows = min(32, p.L - l0);
+#pragma unroll 1
+                for (int u = 0; u < nrows; ++u) {
+                    // p of depth row l0 + u lives in thread (u % 16), slot u / 16 of this half-warp
+                    const float pu = __shfl_sync(0xffffffffu, u < 16 ? p0 : p1, (tid & 16) + (u & 15));
+                    if (!valid) continue;
+                    const float* vr = vdb + (row0 + l0 + u) * p.vd.strides[2] + tx * OC;
+#pragma unroll
+                    for (int c = 0; c < OC; c += 2) {
+                        if (tx * OC + c < d) {  // d is a multiple of 4: the pair is in range
+                            const float2 vv = *reinterpret_cast<const float2*>(vr + c);
+                            o[i][c] = fmaf(pu, vv.x, o[i][c]);
+                            o[i][c + 1] = fmaf(pu, vv.y, o[i][c + 1]);
+                        }
+                    }
+                }
+            }
+        }
+    }
+
+    // ---- 2. causal key tiles
+#pragma unroll 1
+    for (int kt = 0; kt < nkt; ++kt) {
+        f32_cp_wait<1>();  // this tile's K (its V may still be in flight)
+        __syncthreads();
+        float s[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) s[i][j] = 0.f;
+#pragma unroll 4
+        for (int c = 0; c < HD; c += 4) {
+            float4 qv[4], kv[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) qv[i] = *reinterpret_cast<const float4*>(sQ + (ty + 32 * i) * C::kStride + c);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) kv[j] = *reinterpret_cast<const float4*>(sK + (tx + 16 * j) * C::kStride + c);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    s[i][j] = fmaf(qv[i].x, kv[j].x, s[i][j]);
+                    s[i][j] = fmaf(qv[i].y, kv[j].y, s[i][j]);
+                    s[i][j] = fmaf(qv[i].z, kv[j].z, s[i][j]);
+                    s[i][j] = fmaf(qv[i].w, kv[j].w, s[i][j]);
+                }
+        }
+        __syncthreads();  // every thread is done with this K tile
+        if (kt + 1 < nkt) stage(sK, kb, p.k.strides[2], (kt + 1) * kF32Keys, kF32Keys, p.T);
+        f32_cp_commit();
+        // online softmax over this tile; keys after the row's token are masked
+        const bool diag = kt * kF32Keys + kF32Keys - 1 > t0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int ti = t0 + ty + 32 * i;
+            float mx = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int kj = kt * kF32Keys + tx + 16 * j;
+                s[i][j] = (diag && kj > ti) ? -INFINITY : s[i][j] * sc;
+                mx = fmaxf(mx, s[i][j]);
+            }
+#pragma unroll
+            for (int off = 1; off < 16; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+            const float m_new = fmaxf(m[i], mx);
+            const float mb = m_new == -INFINITY ? 0.f : m_new;
+            const float alpha = ex2(m[i] - mb);
+            float ps = 0.f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float pj = ex2(s[i][j] - mb);
+                ps += pj;
+                sP[(ty + 32 * i) * (kF32Keys + 4) + tx + 16 * j] = pj;
+            }
+            l[i] = fmaf(l[i], alpha, ps);
+            m[i] = m_new;
+#pragma unroll
+            for (int c = 0; c < OC; ++c) o[i][c] *= alpha;
+        }
+        f32_cp_wait<1>();  // this tile's V (the next K may still be in flight)
+        __syncthreads();   // and P from every thread
+#pragma unroll 2
+        for (int k = 0; k < kF32Keys; k += 4) {
+            float4 pv[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) pv[i] = *reinterpret_cast<const float4*>(sP + (ty + 32 * i) * (kF32Keys + 4) + k);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+                const float* vr = sV + (k + kk) * C::kStride + tx * OC;
+                float vv[OC];
+#pragma unroll
+                for (int c = 0; c < OC; c += 2) {
+                    const float2 v2 = *reinterpret_cast<const float2*>(vr + c);
+                    vv[c] = v2.x;
+                    vv[c + 1] = v2.y;
+                }
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float pk = kk == 0 ? pv[i].x : kk == 1 ? pv[i].y : kk == 2 ? pv[i].z : pv[i].w;
+#pragma unroll
+                    for (int c = 0; c < OC; ++c) o[i][c] = fmaf(pk, vv[c], o[i][c]);
+                }
+            }
+        }
+        __syncthreads();  // every thread is done with this V tile and with P
+        if (kt + 1 < nkt) stage(sV, vb, p.v.strides[2], (kt + 1) * kF32Keys, kF32Keys, p.T);
+        f32_cp_commit();
+    }
+    f32_cp_wait<0>();
+
+    // ---- epilogue: O / l, the zero_rows keys, the log-sum-exp
+    float* obase = static_cast<float*>(p.o.ptr) + b * p.o.strides[0] + h * p.o.strides[1];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        float lt = l[i];
+#pragma unroll
+        for (int off = 1; off < 16; off <<= 1) lt += __shfl_xor_sync(0xffffffffu, lt, off);
+        float mf = m[i], a = 1.f;
+        if (p.zero_rows > 0) {  // zero_rows more keys of score 0 whose values are 0
+            mf = fmaxf(m[i], 0.f);
+            a = ex2(m[i] - mf);
+            lt = fmaf(lt, a, static_cast<float>(p.zero_rows) * ex2(-mf));
+        }
+        const int t = t0 + ty + 32 * i;
+        if (t >= p.T) continue;
+        const float inv = a / lt;
+        if (p.lse && tx == 0)  // natural log of sum_j exp(scale * q.k_j)
+            p.lse[(static_cast<int64_t>(b) * p.Hq + h) * p.T + t] = (mf + __log2f(lt)) * kLn2;
+        float* orow = obase + static_cast<int64_t>(t) * p.o.strides[2] + tx * OC;
+#pragma unroll
+        for (int c = 0; c < OC; c += 2)
+            if (tx * OC + c < d) *reinterpret_cast<float2*>(orow + c) = make_float2(o[i][c] * inv, o[i][c + 1] * inv);
+    }
+}
+
+// The tiled fp32 kernel serves d a multiple of 4 up to 128 with unit-stride, 16-byte
+// aligned rows (float4 copies); everything else takes the row kernel.
+static bool f32_tiled_ok(const FwdParams& p) {
+    if (p.dtype != MODA_F32 || p.d % 4 != 0 || p.d > 128) return false;
+    const ModaTensor* ts[6] = {&p.q, &p.k, &p.v, &p.o, &p.kd, &p.vd};
+    const int nts = p.L > 0 ? 6 : 4;
+    for (int i = 0; i < nts; ++i) {
+        const ModaTensor* t = ts[i];
+        if (t->strides[3] != 1 || reinterpret_cast<uintptr_t>(t->ptr) % 16 != 0) return false;
+        for (int j = 0; j < 3; ++j)
+            if (t->sizes[j] > 1 && t->strides[j] % 4 != 0) return false;
+    }
+    return true;
+}
+
+template <int HD>
+static int launch_f32_tiled_hd(const FwdParams& p, cudaStream_t stream) {
+    using C = F32Cfg<HD>;
+    static std::atomic<uint64_t> attr_done{0};
+    if (ensure_smem_attr(attr_done, moda_fwd_f32_tiled_kernel<HD>, C::kBytes) != cudaSuccess) return MODA_ERR_LAUNCH;
+    const dim3 grid((p.T + kF32Rows - 1) / kF32Rows, p.Hq, p.B);
+    moda_fwd_f32_tiled_kernel<HD><<<grid, kF32Threads, C::kBytes, stream>>>(p);
+    return MODA_OK;
+}
+
 int launch_fwd_simt(const FwdParams& p, cudaStream_t stream) {
+    if (f32_tiled_ok(p)) {
+        if (p.d <= 32) return launch_f32_tiled_hd<32>(p, stream);
+        if (p.d <= 64) return launch_f32_tiled_hd<64>(p, stream);
+        return launch_f32_tiled_hd<128>(p, stream);
+    }
     const dim3 grid((p.T + kSimtRows - 1) / kSimtRows, p.Hq, p.B);
     const dim3 block(kSimtRows * 32);
     switch (p.dtype) {
