@@ -19,8 +19,8 @@ PKG = os.path.dirname(HERE)
 REPO = os.path.dirname(PKG)
 OUT_DIR = os.path.join(PKG, "moda", "_lib")
 OUT = os.path.join(OUT_DIR, "libmoda_b200.so")
-SOURCES = ["moda_abi.cu", "moda_fwd_simt.cu", "moda_fwd_tc.cu", "moda_bwd.cu", "moda_bwd_tc.cu",
-           "moda_proj_tc.cu"]
+SOURCES = ["moda_abi.cu", "moda_fwd_simt.cu", "moda_fwd_tc.cu", "moda_bwd.cu", "moda_bwd_f32.cu",
+           "moda_bwd_tc.cu", "moda_proj_tc.cu"]
 HEADERS = ["moda_common.cuh", "moda_internal.h", os.path.join("..", "..", "include", "moda_b200.h")]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -311,6 +311,36 @@ MODA_DEV void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
         : "memory");
 }
 
+// ------------------------------------------------------------------ cp.async, vectors
+// 16-byte cp.async; src_bytes 0 writes zeros and reads nothing
+MODA_DEV void f32_cp16(float* dst, const float* src, int src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
+                 "r"(src_bytes)
+                 : "memory");
+}
+MODA_DEV void f32_cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+MODA_DEV void f32_cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// W consecutive floats (W = 2 or 4) through one 8- or 16-byte access
+template <int W>
+MODA_DEV void f32_ldv(float* dst, const float* src) {
+    if constexpr (W == 4) {
+        const float4 v = *reinterpret_cast<const float4*>(src);
+        dst[0] = v.x, dst[1] = v.y, dst[2] = v.z, dst[3] = v.w;
+    } else {
+        const float2 v = *reinterpret_cast<const float2*>(src);
+        dst[0] = v.x, dst[1] = v.y;
+    }
+}
+template <int W>
+MODA_DEV void f32_stv(float* dst, const float* src, float s) {
+    if constexpr (W == 4)
+        *reinterpret_cast<float4*>(dst) = make_float4(src[0] * s, src[1] * s, src[2] * s, src[3] * s);
+    else
+        *reinterpret_cast<float2*>(dst) = make_float2(src[0] * s, src[1] * s);
+}
+
 // ------------------------------------------------------------------ UMMA descriptors
 // Shared-memory matrix descriptor (sm_100 format, version 1), 128-byte swizzle:
 //   bits  0-13 start address >> 4     bits 16-29 leading byte offset >> 4

@@ -122,9 +122,10 @@ __global__ void __launch_bounds__(kSimtRows * 32)
 //
 // A CTA (512 threads) takes 128 consecutive tokens of one query head. Thread (ty, tx),
 // ty = tid / 16, tx = tid % 16, owns query rows ty + 32i (i < 4) and, of each 64-key
-// tile, keys tx + 16j (j < 4); of the output it owns columns [tx*OC, tx*OC + OC),
-// OC = HD / 16. The 16 threads of a row sit in one half-warp, so row maxima and sums are
-// 4 shuffles. Per CTA:
+// tile, keys tx + 16j (j < 4); of the output it owns OC = HD / 16 columns, in groups of
+// VW = 4 adjacent ones (2 when HD = 32) at column g*16*VW + tx*VW, so the 16 threads of a
+// row read one contiguous segment of a V row per access. The 16 threads of a row sit in
+// one half-warp, so row maxima and sums are 4 shuffles. Per CTA:
 //   1. the depth rows first: for each of its rows, the row's 16 threads take L depth rows
 //      (two per thread per 32-row chunk), compute their scores against Q from shared
 //      memory, softmax them, and accumulate P.V_depth straight into their own O columns;
@@ -133,8 +134,9 @@ __global__ void __launch_bounds__(kSimtRows * 32)
 //      the diagonal tiles masked, online softmax, P through shared memory, O += P V.
 //      K and V tiles arrive by cp.async; the next tile's K is copied during the softmax
 //      and P.V of this one, the next V during the next S.
-// Shared memory rows are padded by 4 floats, so the 16 rows a half-warp reads at one
-// column fall into different banks.
+// Q, K and V rows in shared memory are padded by 4 floats, so the 16 rows a half-warp
+// reads at one column fall into different banks; P rows by 16, so the two rows a warp
+// writes at one key do too.
 constexpr int kF32Rows = 128, kF32Keys = 64, kF32Threads = 512;
 
 template <int HD>
@@ -143,25 +145,20 @@ struct F32Cfg {
     static constexpr int kQ = 0;                                // Q   [128][HD+4]
     static constexpr int kK = kQ + kF32Rows * kStride;          // K   [64][HD+4]
     static constexpr int kV = kK + kF32Keys * kStride;          // V   [64][HD+4]
-    static constexpr int kP = kV + kF32Keys * kStride;          // P   [128][64+4]
-    static constexpr int kFloats = kP + kF32Rows * (kF32Keys + 4);
+    static constexpr int kPStride = kF32Keys + 16;             // a warp's two P rows 16 banks apart
+    static constexpr int kP = kV + kF32Keys * kStride;          // P   [128][64+16]
+    static constexpr int kFloats = kP + kF32Rows * kPStride;
     static constexpr int kBytes = kFloats * 4;
 };
-
-// 16-byte cp.async; src_bytes 0 writes zeros and reads nothing
-MODA_DEV void f32_cp16(float* dst, const float* src, int src_bytes) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
-                 "r"(src_bytes)
-                 : "memory");
-}
-MODA_DEV void f32_cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-MODA_DEV void f32_cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 template <int HD>
 __global__ void __launch_bounds__(kF32Threads, 1) moda_fwd_f32_tiled_kernel(const FwdParams p) {
     using C = F32Cfg<HD>;
+    // a thread's OC output columns: NG groups of VW adjacent columns, group g at column
+    // g*16*VW + tx*VW, so the 16 threads of a row read one contiguous V segment per access
     constexpr int OC = HD / 16;
+    constexpr int VW = OC >= 4 ? 4 : 2;
+    constexpr int NG = OC / VW;
     extern __shared__ __align__(16) float f32_smem[];
     float* sQ = f32_smem + C::kQ;
     float* sK = f32_smem + C::kK;
@@ -256,13 +253,15 @@ __global__ void __launch_bounds__(kF32Threads, 1) moda_fwd_f32_tiled_kernel(cons
                     // p of depth row l0 + u lives in thread (u % 16), slot u / 16 of this half-warp
                     const float pu = __shfl_sync(0xffffffffu, u < 16 ? p0 : p1, (tid & 16) + (u & 15));
                     if (!valid) continue;
-                    const float* vr = vdb + (row0 + l0 + u) * p.vd.strides[2] + tx * OC;
+                    const float* vr = vdb + (row0 + l0 + u) * p.vd.strides[2] + tx * VW;
 #pragma unroll
-                    for (int c = 0; c < OC; c += 2) {
-                        if (tx * OC + c < d) {  // d is a multiple of 4: the pair is in range
-                            const float2 vv = *reinterpret_cast<const float2*>(vr + c);
-                            o[i][c] = fmaf(pu, vv.x, o[i][c]);
-                            o[i][c + 1] = fmaf(pu, vv.y, o[i][c + 1]);
+                    for (int g = 0; g < NG; ++g) {
+                        // d is a multiple of 4: a group that starts below d lies inside it
+                        if (tx * VW + g * 16 * VW < d) {
+                            float vv[VW];
+                            f32_ldv<VW>(vv, vr + g * 16 * VW);
+#pragma unroll
+                            for (int w = 0; w < VW; ++w) o[i][g * VW + w] = fmaf(pu, vv[w], o[i][g * VW + w]);
                         }
                     }
                 }
@@ -322,7 +321,7 @@ __global__ void __launch_bounds__(kF32Threads, 1) moda_fwd_f32_tiled_kernel(cons
             for (int j = 0; j < 4; ++j) {
                 const float pj = ex2(s[i][j] - mb);
                 ps += pj;
-                sP[(ty + 32 * i) * (kF32Keys + 4) + tx + 16 * j] = pj;
+                sP[(ty + 32 * i) * C::kPStride + tx + 16 * j] = pj;
             }
             l[i] = fmaf(l[i], alpha, ps);
             m[i] = m_new;
@@ -335,17 +334,13 @@ __global__ void __launch_bounds__(kF32Threads, 1) moda_fwd_f32_tiled_kernel(cons
         for (int k = 0; k < kF32Keys; k += 4) {
             float4 pv[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) pv[i] = *reinterpret_cast<const float4*>(sP + (ty + 32 * i) * (kF32Keys + 4) + k);
+            for (int i = 0; i < 4; ++i) pv[i] = *reinterpret_cast<const float4*>(sP + (ty + 32 * i) * C::kPStride + k);
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
-                const float* vr = sV + (k + kk) * C::kStride + tx * OC;
+                const float* vr = sV + (k + kk) * C::kStride + tx * VW;
                 float vv[OC];
 #pragma unroll
-                for (int c = 0; c < OC; c += 2) {
-                    const float2 v2 = *reinterpret_cast<const float2*>(vr + c);
-                    vv[c] = v2.x;
-                    vv[c + 1] = v2.y;
-                }
+                for (int g = 0; g < NG; ++g) f32_ldv<VW>(vv + g * VW, vr + g * 16 * VW);
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
                     const float pk = kk == 0 ? pv[i].x : kk == 1 ? pv[i].y : kk == 2 ? pv[i].z : pv[i].w;
@@ -378,10 +373,10 @@ __global__ void __launch_bounds__(kF32Threads, 1) moda_fwd_f32_tiled_kernel(cons
         const float inv = a / lt;
         if (p.lse && tx == 0)  // natural log of sum_j exp(scale * q.k_j)
             p.lse[(static_cast<int64_t>(b) * p.Hq + h) * p.T + t] = (mf + __log2f(lt)) * kLn2;
-        float* orow = obase + static_cast<int64_t>(t) * p.o.strides[2] + tx * OC;
+        float* orow = obase + static_cast<int64_t>(t) * p.o.strides[2] + tx * VW;
 #pragma unroll
-        for (int c = 0; c < OC; c += 2)
-            if (tx * OC + c < d) *reinterpret_cast<float2*>(orow + c) = make_float2(o[i][c] * inv, o[i][c + 1] * inv);
+        for (int g = 0; g < NG; ++g)
+            if (tx * VW + g * 16 * VW < d) f32_stv<VW>(orow + g * 16 * VW, o[i] + g * VW, inv);
     }
 }
 
