@@ -47,6 +47,14 @@ combine kernel), installed unmodified in ``baseline/_ref`` and imported from the
 a separate package name, on the same inputs as the default workload; it also reports
 the largest difference from this library's output.
 
+``--pass reference-train`` (one GPU) times forward + backward through autograd: this
+library's ``moda_attention_cuda`` against the reference's training path, autograd through
+its own ``moda_attention_naive`` (chunked; ``baseline/_ref``, unmodified), same inputs.
+
+``--dtype fp32`` runs ``--pass backward``, ``triton-reference`` or ``reference-train`` on
+fp32 inputs (this library's CUDA-core kernels); ``--batch`` and ``--seq`` shrink B and T
+for those passes.
+
 ``--pass backward`` (one GPU) times the backward kernels instead: one step = the
 gradients of all five inputs for a seeded dO, from the forward's O and row
 log-sum-exp (computed once, untimed). Its algorithmic FLOPs are 2.5x the
@@ -297,6 +305,28 @@ def make_unit_inputs(wl, u_lo, u_hi, device, dtype):
     return Q, K, V, Kd, Vd
 
 
+def resized(wl, batch=None, seq=None):
+    """The workload with B and / or T replaced (same seeds, heads, head_dim, L)."""
+    if batch is None and seq is None:
+        return wl
+    out = dict(wl)
+    out["B"] = batch or wl["B"]
+    out["T"] = seq or wl["T"]
+    out["desc"] = (wl["desc"].split(":")[0] + f": B={out['B']} H_q={wl['Hq']} H_k={wl['Hk']} "
+                   f"T={out['T']} d={wl['d']} L={wl['L']} chunk_size={wl['chunk']}")
+    return out
+
+
+def torch_dtype(name):
+    import torch
+    return {"bf16": torch.bfloat16, "fp32": torch.float32}[name]
+
+
+def fma_peak_tflops(max_mhz):
+    """Nominal fp32 FMA-pipe peak: 148 SMs x 128 lanes x 2 FLOP per clock."""
+    return 148 * 128 * 2 * max_mhz * 1e6 / 1e12 if max_mhz else None
+
+
 def sample_rows(B, Hq, T, G, seed, extra=10):
     """Rows (b, h, t) to check: first and last tokens, query-tile edges (128/G tokens per
     tile: the last token of one tile and the first of the next, at 16k-1 boundaries),
@@ -421,15 +451,28 @@ def main():
     ap.add_argument("--no-scaling-config", action="store_true",
                     help="skip the strong-scaling multi-GPU configuration sub-object")
     ap.add_argument("--pass", dest="which",
-                    choices=["forward", "backward", "model", "proj", "triton-reference", "module"],
+                    choices=["forward", "backward", "model", "proj", "triton-reference", "module",
+                             "reference-train"],
                     default="forward")
-    ap.add_argument("--batch", type=int, default=None, help="batch override for --pass proj")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="batch override for --pass proj / backward / triton-reference / reference-train")
+    ap.add_argument("--seq", type=int, default=None,
+                    help="sequence-length override for --pass backward / triton-reference / reference-train")
+    ap.add_argument("--dtype", choices=["bf16", "fp32"], default="bf16",
+                    help="input dtype for --pass backward / triton-reference / reference-train")
     ap.add_argument("--graph", action="store_true",
                     help="--pass module / model: capture one forward as a CUDA graph and time replays")
     ap.add_argument("--kernel-shares", action="store_true",
                     help="--pass model: also print each path's per-kernel CUDA time (stderr)")
     args = ap.parse_args()
     wl = WORKLOADS[args.workload]
+    side = ("backward", "triton-reference", "reference-train")
+    if args.which in side:
+        wl = resized(wl, args.batch, args.seq)
+        if args.dtype == "fp32":
+            wl = dict(wl, desc=wl["desc"].replace("bf16 fp32-accumulate", "fp32").replace("bf16", "fp32"))
+    elif args.dtype != "bf16" or args.seq is not None:
+        ap.error("--dtype and --seq apply to --pass " + " / ".join(side))
     if args.impl == "reference":
         return run_reference(args, wl)
     if args.which == "backward":
@@ -442,6 +485,8 @@ def main():
         return run_triton_reference(args, wl)
     if args.which == "module":
         return run_module(args)
+    if args.which == "reference-train":
+        return run_reference_train(args, wl)
     args.warmup = max(args.warmup, 3)
 
     import torch
@@ -625,10 +670,11 @@ def run_backward(args, wl):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     B, Hq, Hk, T, d, L, C = wl["B"], wl["Hq"], wl["Hk"], wl["T"], wl["d"], wl["L"], wl["chunk"]
-    Q, K, V, Kd, Vd = make_inputs(wl, 0, B, dev, torch.bfloat16)
+    dt = torch_dtype(args.dtype)
+    Q, K, V, Kd, Vd = make_inputs(wl, 0, B, dev, dt)
     O, lse = moda_forward_lse(Q, K, V, Kd, Vd, L, None, C)
     g = torch.Generator(device=dev).manual_seed(wl["seed"] + 7)
-    dO = torch.randn(Q.shape, device=dev, dtype=torch.bfloat16, generator=g)
+    dO = torch.randn(Q.shape, device=dev, dtype=dt, generator=g)
 
     def step():
         return moda_backward(dO, Q, K, V, Kd, Vd, O, lse, L)
@@ -648,18 +694,24 @@ def run_backward(args, wl):
     f_bwd = 2.5 * flops(B, Hq, T, d, L)
     tflops = f_bwd / (ms_step * 1e-3) / 1e12
     p_tflops, p_gbs, p_kind = peaks()
+    note = "tcgen05 dK/dV and dQ kernels, CUDA-core delta and depth kernels"
+    bound = "tensor"
+    if args.dtype == "fp32":
+        cs = clocks.summary()
+        p_tflops = fma_peak_tflops(cs["sm_max_mhz"]) or float("nan")
+        p_kind, bound = "nominal fp32 FMA pipe at the maximum SM clock", "fma"
+        note = "CUDA-core tiled delta, dq, dkdv and depth kernels (fp32 FMA)"
     finite = all(bool(torch.isfinite(x).all()) for x in grads)
     line = {
         "metric": METRIC_BWD, "value": tflops, "unit": "TFLOP/s", "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": args.dtype,
         "data": "synthetic N(0,1), seeded per batch; dO seeded N(0,1)",
         "config": {"workload": wl["desc"].replace("forward", "backward"), "global_batch": B,
                    "H_q": Hq, "H_k": Hk, "seq_len": T, "head_dim": d, "num_layers": L},
-        "roofline": {"bound": "tensor", "achieved": tflops, "peak": p_tflops, "unit": "TFLOP/s",
+        "roofline": {"bound": bound, "achieved": tflops, "peak": p_tflops, "unit": "TFLOP/s",
                      "frac": tflops / p_tflops, "peak_kind": p_kind, "traffic": None,
-                     "algorithmic_flops": f_bwd,
-                     "note": "tcgen05 dK/dV and dQ kernels, CUDA-core delta and depth kernels"},
+                     "algorithmic_flops": f_bwd, "note": note},
         "gpu_launches": 4 * args.steps,
         "clocks": clocks.summary(),
         "verify": {"finite": finite, "device_status": device_status(dev)},
@@ -885,7 +937,7 @@ def run_triton_reference(args, wl):
     args.warmup = max(args.warmup, 3)
     B, Hq, Hk, T, d, L, C = wl["B"], wl["Hq"], wl["Hk"], wl["T"], wl["d"], wl["L"], wl["chunk"]
     base = {"metric": METRIC, "unit": "TFLOP/s", "n_gpus": 1, "impl": "reference-triton-gpu",
-            "higher_is_better": True, "dtype": "bf16", "data": "synthetic N(0,1), seeded per batch",
+            "higher_is_better": True, "dtype": args.dtype, "data": "synthetic N(0,1), seeded per batch",
             "config": {"workload": wl["desc"]}}
     try:
         ref = load_reference_package()
@@ -897,7 +949,7 @@ def run_triton_reference(args, wl):
     from moda.kernels.moda_cuda import moda_forward_into
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    Q, K, V, Kd, Vd = make_inputs(wl, 0, B, dev, torch.bfloat16)
+    Q, K, V, Kd, Vd = make_inputs(wl, 0, B, dev, torch_dtype(args.dtype))
     stream = torch.cuda.current_stream(dev)
     try:
         for _ in range(args.warmup):
@@ -914,16 +966,79 @@ def run_triton_reference(args, wl):
         print(json.dumps({**base, "unavailable": f"reference Triton path failed: {e!r}"[:300]}))
         return
     ms = e0.elapsed_time(e1) / args.steps
+    del out
     ours = torch.empty_like(Q)
-    moda_forward_into(ours, Q, K, V, Kd, Vd, L, None, C)
+    for _ in range(args.warmup):
+        moda_forward_into(ours, Q, K, V, Kd, Vd, L, None, C)
+    e0.record(stream)
+    for _ in range(args.steps):
+        moda_forward_into(ours, Q, K, V, Kd, Vd, L, None, C)
+    e1.record(stream)
     torch.cuda.synchronize(dev)
+    ms_ours = e0.elapsed_time(e1) / args.steps
+    out = triton_fn(Q, K, V, Kd, Vd, num_layers=L, chunk_size=C)
     diff = (ours.float() - out.float()).abs().max().item()
     tflops = flops(B, Hq, T, d, L) / (ms * 1e-3) / 1e12
     line = {**base, "value": tflops, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms, "scaling": "weak", "vs_baseline": None,
             "tokens_per_s": B * T / (ms * 1e-3),
+            "this_library_ms_per_step": ms_ours, "reference_ms_over_this_library": ms / ms_ours,
             "max_abs_diff_vs_this_library": diff, "clocks": clocks.summary(),
             "verify": {"device_status": device_status(dev)}}
+    print(json.dumps(line), flush=True)
+
+
+def run_reference_train(args, wl):
+    """Forward + backward through autograd on one GPU: this library's moda_attention_cuda
+    against the reference's training path, autograd through its own moda_attention_naive
+    (chunked with the workload's chunk_size; baseline/_ref, unmodified), on the same
+    seeded inputs and dO. Reports both times and the largest gradient difference."""
+    import torch
+    from moda.kernels import device_status, moda_attention_cuda
+    args.warmup = max(args.warmup, 3)
+    B, Hq, Hk, T, d, L, C = wl["B"], wl["Hq"], wl["Hk"], wl["T"], wl["d"], wl["L"], wl["chunk"]
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    dt = torch_dtype(args.dtype)
+    ins = [t.requires_grad_(True) for t in make_inputs(wl, 0, B, dev, dt)]
+    g = torch.Generator(device=dev).manual_seed(wl["seed"] + 7)
+    dO = torch.randn(ins[0].shape, device=dev, dtype=dt, generator=g)
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn):
+        def step():
+            for t in ins:
+                t.grad = None
+            fn(*ins, L, None, C).backward(dO)
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / args.steps, [t.grad.float() for t in ins]
+
+    with ClockSampler(0) as clocks:
+        ms_ours, g_ours = timed(moda_attention_cuda)
+    line = {"metric": "MoDA attention forward + backward through autograd (ms per step)",
+            "value": ms_ours, "unit": "ms", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_ours, "higher_is_better": False,
+            "impl": "ours-vs-reference-autograd", "dtype": args.dtype,
+            "data": "synthetic N(0,1), seeded per batch; dO seeded N(0,1)",
+            "config": {"workload": wl["desc"].replace("forward", "forward + backward")},
+            "clocks": clocks.summary(), "verify": {"device_status": device_status(dev)}}
+    try:
+        ref = load_reference_package()
+        ms_ref, g_ref = timed(ref.kernels.moda_attention_naive)
+        line["reference_ms_per_step"] = ms_ref
+        line["reference_ms_over_this_library"] = ms_ref / ms_ours
+        line["max_rel_grad_diff"] = max(
+            float((a - b).abs().max()) / max(1.0, float(b.abs().max())) for a, b in zip(g_ours, g_ref))
+    except Exception as e:  # noqa: BLE001 -- reported, not hidden
+        line["reference_unavailable"] = f"{type(e).__name__}: {e}"[:300]
     print(json.dumps(line), flush=True)
 
 

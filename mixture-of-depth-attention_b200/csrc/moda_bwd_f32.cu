@@ -144,8 +144,9 @@ __global__ void __launch_bounds__(kB32Threads, 1) moda_bwd_f32_dq_kernel(const _
     float* sdS = sV + C::kRowTile;
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
     const int ntiles = (p.T + kB32Tile - 1) / kB32Tile;
-    const int t0 = (ntiles - 1 - static_cast<int>(blockIdx.x)) * kB32Tile;  // heaviest first
-    const int h = blockIdx.y, b = blockIdx.z, hk = h / p.G, d = p.d;
+    // grid (H_q * B, tiles): every head's heaviest tile (the last 64 tokens) goes first
+    const int t0 = (ntiles - 1 - static_cast<int>(blockIdx.y)) * kB32Tile;
+    const int h = blockIdx.x % p.Hq, b = blockIdx.x / p.Hq, hk = h / p.G, d = p.d;
     const float* kb = b32_head(p.k, b, hk);
     const float* vb = b32_head(p.v, b, hk);
     const float sc2 = p.scale * kLog2e;
@@ -221,8 +222,10 @@ __global__ void __launch_bounds__(kB32Threads, 1) moda_bwd_f32_dkdv_kernel(const
     float* sP = sdO + C::kRowTile;
     float* sdS = sP + C::kPTile;
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
-    const int k0 = blockIdx.x * kB32Tile;  // block 0 has the most query tiles
-    const int hk = blockIdx.y, b = blockIdx.z, d = p.d, G = p.G;
+    // grid (H_k * B, tiles): every KV head's heaviest tile (the first 64 keys, read by
+    // every query tile) goes first
+    const int k0 = blockIdx.y * kB32Tile;
+    const int hk = blockIdx.x % p.Hk, b = blockIdx.x / p.Hk, d = p.d, G = p.G;
     const float sc2 = p.scale * kLog2e;
 
     // query tile idx: tokens tq0 = k0 + (idx / G) * 64 of head hk*G + idx % G
@@ -447,6 +450,7 @@ __global__ void moda_bwd_f32_depth_zero_kernel(const __grid_constant__ BwdParams
 // (float4 copies) in every tensor the kernels read or write with vectors.
 bool f32_bwd_tiled_ok(const BwdParams& p) {
     if (p.dtype != MODA_F32 || p.d % 4 != 0 || p.d > 128 || p.G > 32) return false;
+    if ((p.T + kB32Tile - 1) / kB32Tile > 65535 || static_cast<int64_t>(p.Hq) * p.B > INT32_MAX) return false;
     const ModaTensor* ts[11] = {&p.q, &p.k, &p.v, &p.dout, &p.dq, &p.dk, &p.dv, &p.kd, &p.vd, &p.dkd, &p.dvd};
     const int nts = p.L > 0 ? 11 : 7;
     for (int i = 0; i < nts; ++i) {
@@ -466,8 +470,8 @@ static int launch_b32_hd(const BwdParams& p, cudaStream_t stream) {
         ensure_smem_attr(dkv_attr, moda_bwd_f32_dkdv_kernel<HD>, C::kDkvBytes) != cudaSuccess)
         return MODA_ERR_LAUNCH;
     const unsigned tiles = static_cast<unsigned>((p.T + kB32Tile - 1) / kB32Tile);
-    moda_bwd_f32_dq_kernel<HD><<<dim3(tiles, p.Hq, p.B), kB32Threads, C::kDqBytes, stream>>>(p);
-    moda_bwd_f32_dkdv_kernel<HD><<<dim3(tiles, p.Hk, p.B), kB32Threads, C::kDkvBytes, stream>>>(p);
+    moda_bwd_f32_dq_kernel<HD><<<dim3(p.Hq * p.B, tiles), kB32Threads, C::kDqBytes, stream>>>(p);
+    moda_bwd_f32_dkdv_kernel<HD><<<dim3(p.Hk * p.B, tiles), kB32Threads, C::kDkvBytes, stream>>>(p);
     return MODA_OK;
 }
 

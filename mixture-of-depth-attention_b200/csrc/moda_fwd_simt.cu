@@ -166,8 +166,10 @@ __global__ void __launch_bounds__(kF32Threads, 1) moda_fwd_f32_tiled_kernel(cons
     float* sP = f32_smem + C::kP;
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
     const int ntiles = (p.T + kF32Rows - 1) / kF32Rows;
-    const int t0 = (ntiles - 1 - static_cast<int>(blockIdx.x)) * kF32Rows;  // heaviest first
-    const int h = blockIdx.y, b = blockIdx.z, hk = h / p.G;
+    // grid (H_q * B, tiles): dispatch runs x fastest, so every head's heaviest tile (the
+    // last 128 tokens) goes first, then every head's next one
+    const int t0 = (ntiles - 1 - static_cast<int>(blockIdx.y)) * kF32Rows;
+    const int h = blockIdx.x % p.Hq, b = blockIdx.x / p.Hq, hk = h / p.G;
     const int d = p.d;
     const float* qb = static_cast<const float*>(p.q.ptr) + b * p.q.strides[0] + h * p.q.strides[1];
     const float* kb = static_cast<const float*>(p.k.ptr) + b * p.k.strides[0] + hk * p.k.strides[1];
@@ -384,6 +386,7 @@ __global__ void __launch_bounds__(kF32Threads, 1) moda_fwd_f32_tiled_kernel(cons
 // aligned rows (float4 copies); everything else takes the row kernel.
 static bool f32_tiled_ok(const FwdParams& p) {
     if (p.dtype != MODA_F32 || p.d % 4 != 0 || p.d > 128) return false;
+    if ((p.T + kF32Rows - 1) / kF32Rows > 65535 || static_cast<int64_t>(p.Hq) * p.B > INT32_MAX) return false;
     const ModaTensor* ts[6] = {&p.q, &p.k, &p.v, &p.o, &p.kd, &p.vd};
     const int nts = p.L > 0 ? 6 : 4;
     for (int i = 0; i < nts; ++i) {
@@ -400,7 +403,7 @@ static int launch_f32_tiled_hd(const FwdParams& p, cudaStream_t stream) {
     using C = F32Cfg<HD>;
     static std::atomic<uint64_t> attr_done{0};
     if (ensure_smem_attr(attr_done, moda_fwd_f32_tiled_kernel<HD>, C::kBytes) != cudaSuccess) return MODA_ERR_LAUNCH;
-    const dim3 grid((p.T + kF32Rows - 1) / kF32Rows, p.Hq, p.B);
+    const dim3 grid(p.Hq * p.B, (p.T + kF32Rows - 1) / kF32Rows);
     moda_fwd_f32_tiled_kernel<HD><<<grid, kF32Threads, C::kBytes, stream>>>(p);
     return MODA_OK;
 }
