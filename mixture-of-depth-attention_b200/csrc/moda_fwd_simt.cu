@@ -120,8 +120,8 @@ __global__ void __launch_bounds__(kSimtRows * 32)
 // every query row and reduces every dot product across a warp). fp32 FMA throughout, so
 // the fp32 tolerance holds; only the summation order differs from the row kernel.
 //
-// A CTA (512 threads) takes 128 consecutive tokens of one query head. Thread (ty, tx),
-// ty = tid / 16, tx = tid % 16, owns query rows ty + 32i (i < 4) and, of each 64-key
+// A CTA (256 threads) takes 128 consecutive tokens of one query head. Thread (ty, tx),
+// ty = tid / 16, tx = tid % 16, owns query rows ty + 16i (i < 8) and, of each 64-key
 // tile, keys tx + 16j (j < 4); of the output it owns OC = HD / 16 columns, in groups of
 // VW = 4 adjacent ones (2 when HD = 32) at column g*16*VW + tx*VW, so the 16 threads of a
 // row read one contiguous segment of a V row per access. The 16 threads of a row sit in
@@ -130,14 +130,16 @@ __global__ void __launch_bounds__(kSimtRows * 32)
 //      (two per thread per 32-row chunk), compute their scores against Q from shared
 //      memory, softmax them, and accumulate P.V_depth straight into their own O columns;
 //      this seeds the online softmax (m, l, O);
-//   2. the causal keys in 64-key tiles: S = Q K^T from shared memory (4 x 4 per thread),
+//   2. the causal keys in 64-key tiles: S = Q K^T from shared memory (8 x 4 per thread),
 //      the diagonal tiles masked, online softmax, P through shared memory, O += P V.
 //      K and V tiles arrive by cp.async; the next tile's K is copied during the softmax
 //      and P.V of this one, the next V during the next S.
 // Q, K and V rows in shared memory are padded by 4 floats, so the 16 rows a half-warp
 // reads at one column fall into different banks; P rows by 16, so the two rows a warp
 // writes at one key do too.
-constexpr int kF32Rows = 128, kF32Keys = 64, kF32Threads = 512;
+constexpr int kF32Rows = 128, kF32Keys = 64;
+constexpr int kF32RowsPerThread = 8;  // query rows of a thread's 8 x 4 score block
+__host__ __device__ constexpr int f32_threads(int rpt) { return kF32Rows / rpt * 16; }
 
 template <int HD>
 struct F32Cfg {
@@ -151,9 +153,11 @@ struct F32Cfg {
     static constexpr int kBytes = kFloats * 4;
 };
 
-template <int HD>
-__global__ void __launch_bounds__(kF32Threads, 1) moda_fwd_f32_tiled_kernel(const FwdParams p) {
+template <int HD, int RPT>
+__global__ void __launch_bounds__(f32_threads(RPT), 1) moda_fwd_f32_tiled_kernel(const FwdParams p) {
     using C = F32Cfg<HD>;
+    // RPT query rows per thread, RS apart (RS = 128 / RPT threads per key column)
+    constexpr int NT = f32_threads(RPT), RS = kF32Rows / RPT;
     // a thread's OC output columns: NG groups of VW adjacent columns, group g at column
     // g*16*VW + tx*VW, so the 16 threads of a row read one contiguous V segment per access
     constexpr int OC = HD / 16;
@@ -178,7 +182,7 @@ __global__ void __launch_bounds__(kF32Threads, 1) moda_fwd_f32_tiled_kernel(cons
 
     // stage `rows` rows starting at row0 of a [.., rows, d] view into dst (zeros past T or d)
     auto stage = [&](float* dst, const float* base, int64_t rstride, int row0, int rows, int limit) {
-        for (int i = tid; i < rows * (HD / 4); i += kF32Threads) {
+        for (int i = tid; i < rows * (HD / 4); i += NT) {
             const int r = i / (HD / 4), c4 = i % (HD / 4);
             const bool ok = row0 + r < limit && 4 * c4 < d;
             const float* src = ok ? base + static_cast<int64_t>(row0 + r) * rstride + 4 * c4 : base;
@@ -194,9 +198,9 @@ __global__ void __launch_bounds__(kF32Threads, 1) moda_fwd_f32_tiled_kernel(cons
     stage(sV, vb, p.v.strides[2], 0, kF32Keys, p.T);
     f32_cp_commit();
 
-    float o[4][OC], m[4], l[4];
+    float o[RPT][OC], m[RPT], l[RPT];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < RPT; ++i) {
         m[i] = -INFINITY;
         l[i] = 0.f;
 #pragma unroll
@@ -205,13 +209,13 @@ __global__ void __launch_bounds__(kF32Threads, 1) moda_fwd_f32_tiled_kernel(cons
     f32_cp_wait<2>();  // Q
     __syncthreads();
 
-    // ---- 1. depth rows: row ty + 32i is token t0 + ty + 32i; its 16 threads split the L rows
+    // ---- 1. depth rows: row ty + RS*i is token t0 + ty + RS*i; its 16 threads split the L rows
     if (p.L > 0) {
         const float* kdb = static_cast<const float*>(p.kd.ptr) + b * p.kd.strides[0] + hk * p.kd.strides[1];
         const float* vdb = static_cast<const float*>(p.vd.ptr) + b * p.vd.strides[0] + hk * p.vd.strides[1];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {  // unrolled: o, m and l stay in registers
-            const int r = ty + 32 * i, t = t0 + r;
+        for (int i = 0; i < RPT; ++i) {  // unrolled: o, m and l stay in registers
+            const int r = ty + RS * i, t = t0 + r;
             // rows past T (last tile) run the same shuffles with nothing read or kept: the
             // two rows of a warp must stay converged
             const bool valid = t < p.T;
@@ -276,20 +280,20 @@ __global__ void __launch_bounds__(kF32Threads, 1) moda_fwd_f32_tiled_kernel(cons
     for (int kt = 0; kt < nkt; ++kt) {
         f32_cp_wait<1>();  // this tile's K (its V may still be in flight)
         __syncthreads();
-        float s[4][4];
+        float s[RPT][4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
+        for (int i = 0; i < RPT; ++i)
 #pragma unroll
             for (int j = 0; j < 4; ++j) s[i][j] = 0.f;
 #pragma unroll 4
         for (int c = 0; c < HD; c += 4) {
-            float4 qv[4], kv[4];
+            float4 qv[RPT], kv[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) qv[i] = *reinterpret_cast<const float4*>(sQ + (ty + 32 * i) * C::kStride + c);
+            for (int i = 0; i < RPT; ++i) qv[i] = *reinterpret_cast<const float4*>(sQ + (ty + RS * i) * C::kStride + c);
 #pragma unroll
             for (int j = 0; j < 4; ++j) kv[j] = *reinterpret_cast<const float4*>(sK + (tx + 16 * j) * C::kStride + c);
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
+            for (int i = 0; i < RPT; ++i)
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     s[i][j] = fmaf(qv[i].x, kv[j].x, s[i][j]);
@@ -304,8 +308,8 @@ __global__ void __launch_bounds__(kF32Threads, 1) moda_fwd_f32_tiled_kernel(cons
         // online softmax over this tile; keys after the row's token are masked
         const bool diag = kt * kF32Keys + kF32Keys - 1 > t0;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int ti = t0 + ty + 32 * i;
+        for (int i = 0; i < RPT; ++i) {
+            const int ti = t0 + ty + RS * i;
             float mx = -INFINITY;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
@@ -323,7 +327,7 @@ __global__ void __launch_bounds__(kF32Threads, 1) moda_fwd_f32_tiled_kernel(cons
             for (int j = 0; j < 4; ++j) {
                 const float pj = ex2(s[i][j] - mb);
                 ps += pj;
-                sP[(ty + 32 * i) * C::kPStride + tx + 16 * j] = pj;
+                sP[(ty + RS * i) * C::kPStride + tx + 16 * j] = pj;
             }
             l[i] = fmaf(l[i], alpha, ps);
             m[i] = m_new;
@@ -334,9 +338,9 @@ __global__ void __launch_bounds__(kF32Threads, 1) moda_fwd_f32_tiled_kernel(cons
         __syncthreads();   // and P from every thread
 #pragma unroll 2
         for (int k = 0; k < kF32Keys; k += 4) {
-            float4 pv[4];
+            float4 pv[RPT];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) pv[i] = *reinterpret_cast<const float4*>(sP + (ty + 32 * i) * C::kPStride + k);
+            for (int i = 0; i < RPT; ++i) pv[i] = *reinterpret_cast<const float4*>(sP + (ty + RS * i) * C::kPStride + k);
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
                 const float* vr = sV + (k + kk) * C::kStride + tx * VW;
@@ -344,7 +348,7 @@ __global__ void __launch_bounds__(kF32Threads, 1) moda_fwd_f32_tiled_kernel(cons
 #pragma unroll
                 for (int g = 0; g < NG; ++g) f32_ldv<VW>(vv + g * VW, vr + g * 16 * VW);
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
+                for (int i = 0; i < RPT; ++i) {
                     const float pk = kk == 0 ? pv[i].x : kk == 1 ? pv[i].y : kk == 2 ? pv[i].z : pv[i].w;
 #pragma unroll
                     for (int c = 0; c < OC; ++c) o[i][c] = fmaf(pk, vv[c], o[i][c]);
@@ -360,7 +364,7 @@ __global__ void __launch_bounds__(kF32Threads, 1) moda_fwd_f32_tiled_kernel(cons
     // ---- epilogue: O / l, the zero_rows keys, the log-sum-exp
     float* obase = static_cast<float*>(p.o.ptr) + b * p.o.strides[0] + h * p.o.strides[1];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < RPT; ++i) {
         float lt = l[i];
 #pragma unroll
         for (int off = 1; off < 16; off <<= 1) lt += __shfl_xor_sync(0xffffffffu, lt, off);
@@ -370,7 +374,7 @@ __global__ void __launch_bounds__(kF32Threads, 1) moda_fwd_f32_tiled_kernel(cons
             a = ex2(m[i] - mf);
             lt = fmaf(lt, a, static_cast<float>(p.zero_rows) * ex2(-mf));
         }
-        const int t = t0 + ty + 32 * i;
+        const int t = t0 + ty + RS * i;
         if (t >= p.T) continue;
         const float inv = a / lt;
         if (p.lse && tx == 0)  // natural log of sum_j exp(scale * q.k_j)
@@ -402,9 +406,11 @@ template <int HD>
 static int launch_f32_tiled_hd(const FwdParams& p, cudaStream_t stream) {
     using C = F32Cfg<HD>;
     static std::atomic<uint64_t> attr_done{0};
-    if (ensure_smem_attr(attr_done, moda_fwd_f32_tiled_kernel<HD>, C::kBytes) != cudaSuccess) return MODA_ERR_LAUNCH;
+    constexpr int RPT = kF32RowsPerThread;
+    if (ensure_smem_attr(attr_done, moda_fwd_f32_tiled_kernel<HD, RPT>, C::kBytes) != cudaSuccess)
+        return MODA_ERR_LAUNCH;
     const dim3 grid(p.Hq * p.B, (p.T + kF32Rows - 1) / kF32Rows);
-    moda_fwd_f32_tiled_kernel<HD><<<grid, kF32Threads, C::kBytes, stream>>>(p);
+    moda_fwd_f32_tiled_kernel<HD, RPT><<<grid, f32_threads(RPT), C::kBytes, stream>>>(p);
     return MODA_OK;
 }
 
