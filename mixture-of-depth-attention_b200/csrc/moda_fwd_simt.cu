@@ -223,23 +223,48 @@ __global__ void __launch_bounds__(f32_threads(RPT), 1) moda_fwd_f32_tiled_kernel
             const int64_t row0 = static_cast<int64_t>(valid ? t : 0) * p.L;
 #pragma unroll 1
             for (int l0 = 0; l0 < p.L; l0 += 32) {
-                float s2[2];
+                // scores of depth rows l0 .. l0 + nrows - 1: the row's 16 threads split each
+                // depth row's columns like their O columns (one contiguous segment per
+                // access) and sum the partial dot products over the half-warp; depth row u
+                // stays with thread u % 16, slot u / 16 (a past-T row reads token 0's rows
+                // and keeps nothing)
+                const int nrows = min(32, p.L - l0);
+                float qa[OC];
 #pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                    const int li = l0 + tx + 16 * e;
-                    s2[e] = -INFINITY;
-                    if (valid && li < p.L) {
-                        const float* kr = kdb + (row0 + li) * p.kd.strides[2];
-                        float acc = 0.f;
-                        for (int c = 0; c < d; c += 4) {
-                            const float4 kv = *reinterpret_cast<const float4*>(kr + c);
-                            const float4 qv = *reinterpret_cast<const float4*>(qr + c);
-                            acc = fmaf(qv.x, kv.x, acc);
-                            acc = fmaf(qv.y, kv.y, acc);
-                            acc = fmaf(qv.z, kv.z, acc);
-                            acc = fmaf(qv.w, kv.w, acc);
+                for (int g = 0; g < NG; ++g) f32_ldv<VW>(qa + g * VW, qr + g * 16 * VW + tx * VW);
+                float s2[2] = {-INFINITY, -INFINITY};
+                // 8 depth rows per step: their loads are issued before any of them is used
+#pragma unroll 1
+                for (int u0 = 0; u0 < nrows; u0 += 8) {
+                    float kv[8][OC];
+#pragma unroll
+                    for (int uu = 0; uu < 8; ++uu) {
+                        const bool okr = u0 + uu < nrows;  // the same for the whole warp
+                        const float* kr = kdb + (row0 + l0 + (okr ? u0 + uu : 0)) * p.kd.strides[2] + tx * VW;
+#pragma unroll
+                        for (int g = 0; g < NG; ++g) {
+                            if (okr && tx * VW + g * 16 * VW < d) f32_ldv<VW>(kv[uu] + g * VW, kr + g * 16 * VW);
+                            else
+#pragma unroll
+                                for (int w = 0; w < VW; ++w) kv[uu][g * VW + w] = 0.f;
                         }
-                        s2[e] = acc * sc;
+                    }
+                    float part[8];
+#pragma unroll
+                    for (int uu = 0; uu < 8; ++uu) {
+                        part[uu] = 0.f;
+#pragma unroll
+                        for (int c = 0; c < OC; ++c) part[uu] = fmaf(qa[c], kv[uu][c], part[uu]);
+                    }
+#pragma unroll
+                    for (int off = 1; off < 16; off <<= 1)
+#pragma unroll
+                        for (int uu = 0; uu < 8; ++uu) part[uu] += __shfl_xor_sync(0xffffffffu, part[uu], off);
+#pragma unroll
+                    for (int uu = 0; uu < 8; ++uu) {
+                        const int u = u0 + uu;
+                        if (u < nrows && u == tx) s2[0] = part[uu] * sc;
+                        if (u < nrows && u == tx + 16) s2[1] = part[uu] * sc;
                     }
                 }
                 float mx = fmaxf(s2[0], s2[1]);
@@ -253,22 +278,29 @@ __global__ void __launch_bounds__(f32_threads(RPT), 1) moda_fwd_f32_tiled_kernel
                 if (valid) m[i] = m_new;
 #pragma unroll
                 for (int c = 0; c < OC; ++c) o[i][c] *= alpha;
-                const int nrows = min(32, p.L - l0);
 #pragma unroll 1
-                for (int u = 0; u < nrows; ++u) {
-                    // p of depth row l0 + u lives in thread (u % 16), slot u / 16 of this half-warp
-                    const float pu = __shfl_sync(0xffffffffu, u < 16 ? p0 : p1, (tid & 16) + (u & 15));
-                    if (!valid) continue;
-                    const float* vr = vdb + (row0 + l0 + u) * p.vd.strides[2] + tx * VW;
+                for (int u0 = 0; u0 < nrows; u0 += 8) {
+                    float vv[8][OC];
 #pragma unroll
-                    for (int g = 0; g < NG; ++g) {
-                        // d is a multiple of 4: a group that starts below d lies inside it
-                        if (tx * VW + g * 16 * VW < d) {
-                            float vv[VW];
-                            f32_ldv<VW>(vv, vr + g * 16 * VW);
+                    for (int uu = 0; uu < 8; ++uu) {
+                        const bool okr = valid && u0 + uu < nrows;
+                        const float* vr = vdb + (row0 + l0 + (okr ? u0 + uu : 0)) * p.vd.strides[2] + tx * VW;
 #pragma unroll
-                            for (int w = 0; w < VW; ++w) o[i][g * VW + w] = fmaf(pu, vv[w], o[i][g * VW + w]);
+                        for (int g = 0; g < NG; ++g) {
+                            if (okr && tx * VW + g * 16 * VW < d) f32_ldv<VW>(vv[uu] + g * VW, vr + g * 16 * VW);
+                            else
+#pragma unroll
+                                for (int w = 0; w < VW; ++w) vv[uu][g * VW + w] = 0.f;
                         }
+                    }
+#pragma unroll
+                    for (int uu = 0; uu < 8; ++uu) {
+                        // p of depth row u lives in thread (u % 16), slot u / 16 of this
+                        // half-warp; rows at or past nrows have p = 0 and zero values
+                        const int u = u0 + uu;
+                        const float pu = __shfl_sync(0xffffffffu, u < 16 ? p0 : p1, (tid & 16) + (u & 15));
+#pragma unroll
+                        for (int c = 0; c < OC; ++c) o[i][c] = fmaf(pu, vv[uu][c], o[i][c]);
                     }
                 }
             }
