@@ -24,8 +24,6 @@
 // fp32 arithmetic throughout; inputs and gradients in the forward's dtype.
 #include "moda_internal.h"
 
-#include <mutex>
-
 namespace moda {
 
 namespace {
@@ -231,20 +229,10 @@ static void launch_bwd_t(const BwdParams& p, cudaStream_t stream) {
 // part of the library image, so that entry point allocates nothing.
 static __device__ __align__(256) float g_noalloc_delta[MODA_NOALLOC_ROWS];
 
+// Looked up on every call (cheap next to the launches): an address kept from an earlier
+// call would dangle after the context that loaded the module is reset or recreated.
 cudaError_t noalloc_scratch(void** ptr) {
-    static std::mutex mu;
-    static void* addr[kMaxDevices] = {};
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return e;
-    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
-    std::lock_guard<std::mutex> lock(mu);
-    if (!addr[dev]) {
-        e = cudaGetSymbolAddress(&addr[dev], g_noalloc_delta);  // once per device
-        if (e != cudaSuccess) return e;
-    }
-    *ptr = addr[dev];
-    return cudaSuccess;
+    return cudaGetSymbolAddress(ptr, g_noalloc_delta);
 }
 
 template <typename T>

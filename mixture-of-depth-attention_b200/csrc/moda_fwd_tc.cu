@@ -710,7 +710,7 @@ __global__ void __launch_bounds__(kThreads, 1) moda_fwd_tc_kernel(const __grid_c
             const bool valid = tok < ti.tend;
             const int head = it.hk * p.G + row % p.G;
             if (p.lse && half == 0 && valid)  // natural log of sum_j exp(scale * q.k_j)
-                p.lse[(static_cast<long long>(it.b) * p.Hq + head) * p.T + tok] = (m_fin + __log2f(l_tot)) * kLn2;
+                p.lse[it.b * p.lse_sb + head * p.lse_sh + tok] = (m_fin + __log2f(l_tot)) * kLn2;
             uint4* dst = reinterpret_cast<uint4*>(
                 static_cast<uint16_t*>(p.o) + it.b * p.o_sb + head * p.o_sh +
                 static_cast<long long>(tok) * p.o_st + kHalfD * half);
@@ -831,7 +831,9 @@ bool tc_supports(const FwdParams& p, char* why, size_t whylen) {
     };
     if (p.dtype != MODA_BF16 && p.dtype != MODA_F16) return no("tcgen05 path needs bf16 or f16");
     if (p.d != 64 && p.d != 128) return no("tcgen05 path needs head_dim 64 or 128");
-    if (p.G < 1 || p.G > 128 || (128 % p.G) != 0) return no("tcgen05 path needs H_q/H_k dividing 128");
+    // G dividing 128: one launch, 128 / G tokens x G heads per query tile; any other
+    // G <= 128: G launches with G = 1 (launch_fwd_tc)
+    if (p.G < 1 || p.G > 128) return no("tcgen05 path needs 1 <= H_q/H_k <= 128");
     if (!(p.scale > 0.f)) return no("tcgen05 path needs a positive scale");
     if (static_cast<long long>(p.T) * p.L >= (1LL << 31)) return no("T*L too large for TMA coordinates");
     const ModaTensor* ts[6] = {&p.q, &p.k, &p.v, &p.o, &p.kd, &p.vd};
@@ -876,7 +878,8 @@ int sm_count() {
     return n;
 }
 
-int launch_fwd_tc(const FwdParams& p, cudaStream_t stream, char* err, size_t errlen) {
+static int launch_fwd_tc_one(const FwdParams& p, float* lse, long long lse_sb, long long lse_sh,
+                             cudaStream_t stream, char* err, size_t errlen) {
     TcParams tp;
     const CUtensorMapDataType dt =
         p.dtype == MODA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -903,7 +906,9 @@ int launch_fwd_tc(const FwdParams& p, cudaStream_t stream, char* err, size_t err
     tp.n_tok = n_tok;
     tp.num_pairs = (p.T + 2 * n_tok - 1) / (2 * n_tok);
     tp.sc = p.scale * kLog2e;
-    tp.lse = p.lse;
+    tp.lse = lse;
+    tp.lse_sb = lse_sb;
+    tp.lse_sh = lse_sh;
     tp.zero_rows = p.zero_rows;
     const long long items = static_cast<long long>(tp.num_pairs) * p.B * p.Hk;
     if (items == 0) return MODA_OK;
@@ -926,4 +931,30 @@ int launch_fwd_tc(const FwdParams& p, cudaStream_t stream, char* err, size_t err
     return g8 ? launch_tc_inst<64, 0, 8>(tp, g, stream) : launch_tc_inst<64, 0, 16>(tp, g, stream);
 }
 
+
+// H_q / H_k = G with 128 % G != 0 (3, 5, 6, 12, ...): a query tile cannot hold whole
+// tokens of all G heads, so run G problems with G = 1. Problem c takes query heads
+// hk*G + c of every KV head -- one stride, G times the head stride, in Q, O and the
+// log-sum-exp rows -- against the same K, V and depth rows. The K/V tiles are then read
+// G times, once per problem.
+int launch_fwd_tc(const FwdParams& p, cudaStream_t stream, char* err, size_t errlen) {
+    const long long lse_sb = static_cast<long long>(p.Hq) * p.T, lse_sh = p.T;
+    if (128 % p.G == 0) return launch_fwd_tc_one(p, p.lse, lse_sb, lse_sh, stream, err, errlen);
+    const int esz = 2;  // bf16 / f16
+    for (int c = 0; c < p.G; ++c) {
+        FwdParams pc = p;
+        pc.q.ptr = static_cast<char*>(p.q.ptr) + static_cast<long long>(c) * p.q.strides[1] * esz;
+        pc.q.sizes[1] = p.Hk;
+        pc.q.strides[1] = p.q.strides[1] * p.G;
+        pc.o.ptr = static_cast<char*>(p.o.ptr) + static_cast<long long>(c) * p.o.strides[1] * esz;
+        pc.o.sizes[1] = p.Hk;
+        pc.o.strides[1] = p.o.strides[1] * p.G;
+        pc.Hq = p.Hk;
+        pc.G = 1;
+        const int r = launch_fwd_tc_one(pc, p.lse ? p.lse + static_cast<long long>(c) * p.T : nullptr,
+                                        lse_sb, lse_sh * p.G, stream, err, errlen);
+        if (r != MODA_OK) return r;
+    }
+    return MODA_OK;
+}
 }  // namespace moda

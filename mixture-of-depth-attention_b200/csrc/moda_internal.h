@@ -47,7 +47,8 @@ struct TcParams {
     int num_pairs;  // tile pairs per (b, kv head)
     int num_items;  // num_pairs * B * Hk work items
     float sc;       // scale * log2(e)
-    float* lse;     // optional [B, H_q, T] fp32 log-sum-exp output
+    float* lse;     // optional fp32 log-sum-exp output: row (b, head, t) at
+    long long lse_sb, lse_sh;  // lse[b * lse_sb + head * lse_sh + t]
     int zero_rows;  // implicit all-zero depth rows per token (score 0, value 0)
 };
 

@@ -347,3 +347,45 @@ def test_model_config_kernel_shape_through_depth_cache_sampled_rows():
     out = moda_attention_cuda(Q, K, V, Kd, Vd, N, chunk_size=64)
     assert torch.isfinite(out).all()
     _check_sampled(out, Q, K, V, Kd, Vd, N, _boundary_rows(B, Hq, T, Hq // Hk, N, seed=4))
+
+
+# query-head groups that do not divide 128 (H_q / H_k = 3, 5, 6, 12): the tcgen05 kernel
+# runs them as G problems with one query head per KV head
+ODD_G = [(1, 6, 2, 130, 64, 3), (2, 15, 3, 77, 128, 5), (1, 12, 2, 64, 64, 32), (1, 12, 1, 200, 128, 2)]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "f16"])
+@pytest.mark.parametrize("shape", ODD_G, ids=[str(s) for s in ODD_G])
+def test_tc_odd_group_sizes_match_oracle(shape, dtype):
+    from moda.kernels.moda_cuda import moda_forward_into, moda_forward_lse
+    B, Hq, Hk, T, d, L = shape
+    arrs = seeded_inputs(B, Hq, Hk, T, d, L, seed=T + Hq)
+    args = dev(arrs, dtype)
+    assert moda_plan(*args, L) == "tc"
+    rin = rounded(arrs, dtype)
+    ref = orc.moda_attention_naive(*rin, L)
+    assert max_abs(run(args, L, kernel="tc"), ref) <= BF16_ABS_TOL
+    # the row log-sum-exp lands at each head's own rows
+    O, lse = moda_forward_lse(*args, L)
+    lse_ref = orc.moda_attention_grads(*rin, L, np.zeros((B, Hq, T, d)))["lse"]
+    assert max_abs(O.float().cpu().numpy(), ref) <= BF16_ABS_TOL
+    assert max_abs(lse.cpu().numpy(), lse_ref) <= 1e-2 * max(1.0, float(np.abs(lse_ref).max()))
+    # into a [B, T, H_q, d] buffer seen as [B, H_q, T, d]
+    Ot = torch.zeros(B, T, Hq, d, dtype=dtype, device="cuda").transpose(1, 2)
+    moda_forward_into(Ot, *args, L, kernel="tc")
+    assert max_abs(Ot.float().cpu().numpy(), ref) <= BF16_ABS_TOL
+
+
+def test_tc_odd_group_gradients_match_oracle():
+    # the backward reads the forward's log-sum-exp rows, so this also checks where the
+    # G launches put them
+    B, Hq, Hk, T, d, L = 1, 6, 2, 70, 64, 3
+    arrs = seeded_inputs(B, Hq, Hk, T, d, L, seed=5)
+    ins = [t.requires_grad_(True) for t in dev(arrs, torch.bfloat16)]
+    dO = np.random.default_rng(6).standard_normal((B, Hq, T, d))
+    moda_attention_cuda(*ins, L).backward(torch.from_numpy(dO).to("cuda", torch.bfloat16))
+    g = orc.moda_attention_grads(*rounded(arrs, torch.bfloat16), L,
+                                 torch.from_numpy(dO).to(torch.bfloat16).double().numpy())
+    for t, k in zip(ins, ("dQ", "dK", "dV", "dK_depth", "dV_depth")):
+        e = float(np.abs(t.grad.double().cpu().numpy() - g[k]).max()) / max(1.0, float(np.abs(g[k]).max()))
+        assert e <= 3e-2, (k, e)
