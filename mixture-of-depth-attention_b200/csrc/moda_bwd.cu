@@ -243,8 +243,9 @@ static void launch_delta_t(const BwdParams& p, cudaStream_t stream) {
 
 // bf16/f16 with d in {64, 128}, H_q/H_k dividing 128 and TMA-friendly layouts: the
 // sequence part on tensor cores (moda_bwd_tc.cu) and the depth part per token;
-// fp32 with d <= 128 (d % 4 == 0), G <= 32 and 16-byte aligned rows in CUDA-core tiles
-// (moda_bwd_f32.cu); everything else on the CUDA-core row kernels above.
+// the rest with d <= 128 (d % 4 == 0), G <= 32 and 16-byte aligned rows (fp32, and 16-bit
+// shapes the tensor-core kernels do not take) in CUDA-core tiles (moda_bwd_f32.cu);
+// everything else on the CUDA-core row kernels above.
 int launch_bwd(const BwdParams& p, cudaStream_t stream, char* err, size_t errlen) {
     char why[160];
     if (tc_bwd_supports(p, why, sizeof(why))) {
@@ -254,9 +255,13 @@ int launch_bwd(const BwdParams& p, cudaStream_t stream, char* err, size_t errlen
         if (r != MODA_OK) return r;
         return launch_bwd_depth(p, stream);
     }
-    if (f32_bwd_tiled_ok(p)) {  // fp32 in tiles (moda_bwd_f32.cu)
-        if (p.T > 0) launch_delta_t<float>(p, stream);
-        return launch_bwd_f32_tiled(p, stream);
+    if (bwd_tiled_ok(p)) {  // CUDA-core tiles (moda_bwd_f32.cu)
+        if (p.T > 0) {
+            if (p.dtype == MODA_F32) launch_delta_t<float>(p, stream);
+            else if (p.dtype == MODA_BF16) launch_delta_t<__nv_bfloat16>(p, stream);
+            else launch_delta_t<__half>(p, stream);
+        }
+        return launch_bwd_tiled(p, stream);
     }
     switch (p.dtype) {
         case MODA_F32: launch_bwd_t<float>(p, stream); break;

@@ -1,4 +1,8 @@
-// fp32 MoDA backward on CUDA cores, tiled like the fp32 forward (moda_fwd_simt.cu).
+// MoDA backward on CUDA cores in fp32 arithmetic, tiled like the fp32 forward
+// (moda_fwd_simt.cu): fp32 inputs, and bf16 / f16 inputs of the shapes the tensor-core
+// backward does not take (head_dim outside {64, 128}, H_q / H_k not dividing 128).
+// 16-bit rows are staged raw by cp.async and converted once per tile into the fp32
+// tiles; gradients are rounded to the input dtype on store.
 //
 // The gradients are those of moda_bwd.cu's row kernels -- torch autograd of
 // moda_attention_naive (moda/kernels/moda_naive.py:13-162) -- computed from shared-memory
@@ -25,6 +29,7 @@
 #include "moda_internal.h"
 
 #include <algorithm>
+#include <type_traits>
 
 namespace moda {
 
@@ -42,6 +47,82 @@ struct B32Cfg {
 };
 
 namespace {
+
+template <typename T>
+constexpr bool kIsF32 = std::is_same<T, float>::value;
+
+template <typename T>
+MODA_DEV float2 unpack2(uint32_t w);  // two 16-bit values, low half first
+template <>
+MODA_DEV float2 unpack2<__nv_bfloat16>(uint32_t w) {
+    return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+template <>
+MODA_DEV float2 unpack2<__half>(uint32_t w) {
+    return make_float2(__half2float(__ushort_as_half(static_cast<unsigned short>(w & 0xffffu))),
+                       __half2float(__ushort_as_half(static_cast<unsigned short>(w >> 16))));
+}
+template <typename T>
+MODA_DEV uint32_t pack2(float lo, float hi);
+template <>
+MODA_DEV uint32_t pack2<__nv_bfloat16>(float lo, float hi) { return pack_bf16x2(lo, hi); }
+template <>
+MODA_DEV uint32_t pack2<__half>(float lo, float hi) { return pack_f16x2(lo, hi); }
+
+// 4 consecutive elements as floats / from floats times s (16-bit: one 8-byte access)
+template <typename T>
+MODA_DEV float4 b32_ld4(const T* src) {
+    if constexpr (kIsF32<T>) {
+        return *reinterpret_cast<const float4*>(src);
+    } else {
+        const uint2 w = *reinterpret_cast<const uint2*>(src);
+        const float2 a = unpack2<T>(w.x), c = unpack2<T>(w.y);
+        return make_float4(a.x, a.y, c.x, c.y);
+    }
+}
+template <typename T>
+MODA_DEV void b32_st4(T* dst, float4 v, float s) {
+    if constexpr (kIsF32<T>)
+        *reinterpret_cast<float4*>(dst) = make_float4(v.x * s, v.y * s, v.z * s, v.w * s);
+    else
+        *reinterpret_cast<uint2*>(dst) = make_uint2(pack2<T>(v.x * s, v.y * s), pack2<T>(v.z * s, v.w * s));
+}
+
+// 4 elements into 4 floats of shared memory (zeros when !ok): fp32 by cp.async, 16-bit
+// by one 8-byte load and a conversion
+template <typename T>
+MODA_DEV void b32_stage4(float* dst, const T* src, bool ok) {
+    if constexpr (kIsF32<T>) {
+        f32_cp16(dst, src, ok ? 16 : 0);
+    } else {
+        *reinterpret_cast<float4*>(dst) = ok ? b32_ld4<T>(src) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+}
+
+// 64 rows of a [.., rows, d] 16-bit view, from row0, into a raw [64][HD] tile by cp.async
+// (16 bytes = 8 elements per copy; zeros for rows at or past `limit` and columns at or
+// past d)
+template <typename T, int HD>
+MODA_DEV void b16_stage(T* dst, const T* base, int64_t rstride, int row0, int limit, int d, int tid) {
+    for (int i = tid; i < kB32Tile * (HD / 8); i += kB32Threads) {
+        const int r = i / (HD / 8), col = 8 * (i % (HD / 8));
+        const int n = row0 + r < limit && col < d ? min(8, d - col) : 0;  // elements to copy
+        const T* src = n ? base + static_cast<int64_t>(row0 + r) * rstride + col : base;
+        f32_cp16(reinterpret_cast<float*>(dst + r * HD + col), reinterpret_cast<const float*>(src), 2 * n);
+    }
+}
+
+// raw [64][HD] 16-bit tile -> fp32 [64][HD+4] tile
+template <typename T, int HD>
+MODA_DEV void b16_convert(float* dst, const T* raw, int tid) {
+    for (int i = tid; i < kB32Tile * (HD / 8); i += kB32Threads) {
+        const int r = i / (HD / 8), col = 8 * (i % (HD / 8));
+        const uint4 w = *reinterpret_cast<const uint4*>(raw + r * HD + col);
+        const float2 a = unpack2<T>(w.x), b = unpack2<T>(w.y), c = unpack2<T>(w.z), e = unpack2<T>(w.w);
+        *reinterpret_cast<float4*>(dst + r * (HD + 4) + col) = make_float4(a.x, a.y, b.x, b.y);
+        *reinterpret_cast<float4*>(dst + r * (HD + 4) + col + 4) = make_float4(c.x, c.y, e.x, e.y);
+    }
+}
 
 // 64 rows of a [.., rows, d] fp32 view, from row0, into dst [64][HD+4] by cp.async
 // (zeros for rows at or past `limit` and for columns at or past d)
@@ -110,29 +191,38 @@ MODA_DEV void b32_pm(float (&acc)[4][HD / 16], const float* P, const float* M, i
 }
 
 // rows row0 + ty + 16i (those below `rows`) of acc * s into out, this thread's columns
-template <int HD>
+template <typename T, int HD>
 MODA_DEV void b32_store(const ModaTensor& t, int b, int h, int row0, int rows, int d,
                         const float (&acc)[4][HD / 16], float s, int ty, int tx) {
     constexpr int OC = HD / 16, VW = OC >= 4 ? 4 : 2, NG = OC / VW;
-    float* base = static_cast<float*>(t.ptr) + b * t.strides[0] + h * t.strides[1];
+    T* base = static_cast<T*>(t.ptr) + b * t.strides[0] + h * t.strides[1];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const int r = row0 + ty + 16 * i;
         if (r >= rows) continue;
-        float* row = base + static_cast<int64_t>(r) * t.strides[2] + tx * VW;
+        T* row = base + static_cast<int64_t>(r) * t.strides[2] + tx * VW;
 #pragma unroll
-        for (int g = 0; g < NG; ++g)  // d is a multiple of 4: a group starting below d is inside it
-            if (tx * VW + g * 16 * VW < d) f32_stv<VW>(row + g * 16 * VW, acc[i] + g * VW, s);
+        for (int g = 0; g < NG; ++g) {  // d is a multiple of 4: a group starting below d is inside it
+            if (tx * VW + g * 16 * VW >= d) continue;
+            const float* a = acc[i] + g * VW;
+            if constexpr (VW == 4)
+                b32_st4<T>(row + g * 16 * VW, make_float4(a[0], a[1], a[2], a[3]), s);
+            else if constexpr (kIsF32<T>)
+                f32_stv<2>(row + g * 16 * VW, a, s);
+            else
+                *reinterpret_cast<uint32_t*>(row + g * 16 * VW) = pack2<T>(a[0] * s, a[1] * s);
+        }
     }
 }
 
-MODA_DEV const float* b32_head(const ModaTensor& t, int b, int h) {
-    return static_cast<const float*>(t.ptr) + b * t.strides[0] + h * t.strides[1];
+template <typename T>
+MODA_DEV const T* b32_head(const ModaTensor& t, int b, int h) {
+    return static_cast<const T*>(t.ptr) + b * t.strides[0] + h * t.strides[1];
 }
 
 }  // namespace
 
-template <int HD>
+template <typename T, int HD>
 __global__ void __launch_bounds__(kB32Threads, 1) moda_bwd_f32_dq_kernel(const __grid_constant__ BwdParams p) {
     using C = B32Cfg<HD>;
     constexpr int OC = HD / 16;
@@ -142,22 +232,39 @@ __global__ void __launch_bounds__(kB32Threads, 1) moda_bwd_f32_dq_kernel(const _
     float* sK = sdO + C::kRowTile;
     float* sV = sK + C::kRowTile;
     float* sdS = sV + C::kRowTile;
+    T* rK = reinterpret_cast<T*>(sdS + C::kPTile);  // 16-bit only: raw K and V tiles
+    T* rV = rK + kB32Tile * HD;
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
     const int ntiles = (p.T + kB32Tile - 1) / kB32Tile;
     // grid (H_q * B, tiles): every head's heaviest tile (the last 64 tokens) goes first
     const int t0 = (ntiles - 1 - static_cast<int>(blockIdx.y)) * kB32Tile;
     const int h = blockIdx.x % p.Hq, b = blockIdx.x / p.Hq, hk = h / p.G, d = p.d;
-    const float* kb = b32_head(p.k, b, hk);
-    const float* vb = b32_head(p.v, b, hk);
+    const T* kb = b32_head<T>(p.k, b, hk);
+    const T* vb = b32_head<T>(p.v, b, hk);
     const float sc2 = p.scale * kLog2e;
 
-    b32_stage<HD>(sQ, b32_head(p.q, b, h), p.q.strides[2], t0, p.T, d, tid);
-    b32_stage<HD>(sdO, b32_head(p.dout, b, h), p.dout.strides[2], t0, p.T, d, tid);
-    f32_cp_commit();
-    b32_stage<HD>(sV, vb, p.v.strides[2], 0, p.T, d, tid);
-    f32_cp_commit();
-    b32_stage<HD>(sK, kb, p.k.strides[2], 0, p.T, d, tid);
-    f32_cp_commit();
+    if constexpr (kIsF32<T>) {
+        b32_stage<HD>(sQ, b32_head<float>(p.q, b, h), p.q.strides[2], t0, p.T, d, tid);
+        b32_stage<HD>(sdO, b32_head<float>(p.dout, b, h), p.dout.strides[2], t0, p.T, d, tid);
+        f32_cp_commit();
+        b32_stage<HD>(sV, vb, p.v.strides[2], 0, p.T, d, tid);
+        f32_cp_commit();
+        b32_stage<HD>(sK, kb, p.k.strides[2], 0, p.T, d, tid);
+        f32_cp_commit();
+    } else {  // Q and dO through the raw K / V tiles, then K and V of the first key tile
+        b16_stage<T, HD>(rK, b32_head<T>(p.q, b, h), p.q.strides[2], t0, p.T, d, tid);
+        b16_stage<T, HD>(rV, b32_head<T>(p.dout, b, h), p.dout.strides[2], t0, p.T, d, tid);
+        f32_cp_commit();
+        f32_cp_wait<0>();
+        __syncthreads();
+        b16_convert<T, HD>(sQ, rK, tid);
+        b16_convert<T, HD>(sdO, rV, tid);
+        __syncthreads();
+        b16_stage<T, HD>(rV, vb, p.v.strides[2], 0, p.T, d, tid);
+        f32_cp_commit();
+        b16_stage<T, HD>(rK, kb, p.k.strides[2], 0, p.T, d, tid);
+        f32_cp_commit();
+    }
 
     // rows past T: lse = +inf makes their P (and dS) zero
     float lse2[4], del[4];
@@ -178,14 +285,29 @@ __global__ void __launch_bounds__(kB32Threads, 1) moda_bwd_f32_dq_kernel(const _
     const int nkt = (kmax + kB32Tile - 1) / kB32Tile;
 #pragma unroll 1
     for (int kt = 0; kt < nkt; ++kt) {
-        f32_cp_wait<1>();  // Q, dO and this V (this K may still be in flight)
+        f32_cp_wait<1>();  // this V (this K may still be in flight)
         __syncthreads();
+        if constexpr (!kIsF32<T>) {
+            b16_convert<T, HD>(sV, rV, tid);
+            __syncthreads();
+            if (kt + 1 < nkt) b16_stage<T, HD>(rV, vb, p.v.strides[2], (kt + 1) * kB32Tile, p.T, d, tid);
+            f32_cp_commit();
+        }
         float dp[4][4];
         b32_abt<HD>(dp, sdO, sV, ty, tx);
-        f32_cp_wait<0>();  // this K
-        __syncthreads();   // and every thread is done with V
-        if (kt + 1 < nkt) b32_stage<HD>(sV, vb, p.v.strides[2], (kt + 1) * kB32Tile, p.T, d, tid);
-        f32_cp_commit();
+        if constexpr (kIsF32<T>) {
+            f32_cp_wait<0>();  // this K
+            __syncthreads();   // and every thread is done with V
+            if (kt + 1 < nkt) b32_stage<HD>(sV, vb, p.v.strides[2], (kt + 1) * kB32Tile, p.T, d, tid);
+            f32_cp_commit();
+        } else {
+            f32_cp_wait<1>();  // this K (the next V may still be in flight)
+            __syncthreads();
+            b16_convert<T, HD>(sK, rK, tid);
+            __syncthreads();
+            if (kt + 1 < nkt) b16_stage<T, HD>(rK, kb, p.k.strides[2], (kt + 1) * kB32Tile, p.T, d, tid);
+            f32_cp_commit();
+        }
         float s[4][4];
         b32_abt<HD>(s, sQ, sK, ty, tx);
         // keys after a row's token are masked (this covers keys at or past T for rows < T)
@@ -203,14 +325,16 @@ __global__ void __launch_bounds__(kB32Threads, 1) moda_bwd_f32_dq_kernel(const _
         __syncthreads();
         b32_pm<HD>(acc, sdS, sK, ty, tx);
         __syncthreads();  // every thread is done with K and dS
-        if (kt + 1 < nkt) b32_stage<HD>(sK, kb, p.k.strides[2], (kt + 1) * kB32Tile, p.T, d, tid);
-        f32_cp_commit();
+        if constexpr (kIsF32<T>) {
+            if (kt + 1 < nkt) b32_stage<HD>(sK, kb, p.k.strides[2], (kt + 1) * kB32Tile, p.T, d, tid);
+            f32_cp_commit();
+        }
     }
     f32_cp_wait<0>();
-    b32_store<HD>(p.dq, b, h, t0, p.T, d, acc, p.scale, ty, tx);
+    b32_store<T, HD>(p.dq, b, h, t0, p.T, d, acc, p.scale, ty, tx);
 }
 
-template <int HD>
+template <typename T, int HD>
 __global__ void __launch_bounds__(kB32Threads, 1) moda_bwd_f32_dkdv_kernel(const __grid_constant__ BwdParams p) {
     using C = B32Cfg<HD>;
     constexpr int OC = HD / 16;
@@ -221,6 +345,8 @@ __global__ void __launch_bounds__(kB32Threads, 1) moda_bwd_f32_dkdv_kernel(const
     float* sdO = sQ + C::kRowTile;
     float* sP = sdO + C::kRowTile;
     float* sdS = sP + C::kPTile;
+    T* rQ = reinterpret_cast<T*>(sdS + C::kPTile);  // 16-bit only: raw Q and dO tiles
+    T* rO = rQ + kB32Tile * HD;
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
     // grid (H_k * B, tiles): every KV head's heaviest tile (the first 64 keys, read by
     // every query tile) goes first
@@ -230,16 +356,29 @@ __global__ void __launch_bounds__(kB32Threads, 1) moda_bwd_f32_dkdv_kernel(const
 
     // query tile idx: tokens tq0 = k0 + (idx / G) * 64 of head hk*G + idx % G
     const int nq = (p.T - k0 + kB32Tile - 1) / kB32Tile * G;
-    auto stage_q = [&](float* dst, const ModaTensor& t, int idx) {
-        b32_stage<HD>(dst, b32_head(t, b, hk * G + idx % G), t.strides[2], k0 + idx / G * kB32Tile, p.T, d,
-                      tid);
+    auto stage_q = [&](float* dst, T* raw, const ModaTensor& t, int idx) {
+        const T* base = b32_head<T>(t, b, hk * G + idx % G);
+        const int row0 = k0 + idx / G * kB32Tile;
+        if constexpr (kIsF32<T>) b32_stage<HD>(dst, base, t.strides[2], row0, p.T, d, tid);
+        else b16_stage<T, HD>(raw, base, t.strides[2], row0, p.T, d, tid);
     };
-    b32_stage<HD>(sK, b32_head(p.k, b, hk), p.k.strides[2], k0, p.T, d, tid);
-    b32_stage<HD>(sV, b32_head(p.v, b, hk), p.v.strides[2], k0, p.T, d, tid);
+    if constexpr (kIsF32<T>) {
+        b32_stage<HD>(sK, b32_head<float>(p.k, b, hk), p.k.strides[2], k0, p.T, d, tid);
+        b32_stage<HD>(sV, b32_head<float>(p.v, b, hk), p.v.strides[2], k0, p.T, d, tid);
+        f32_cp_commit();
+    } else {  // K and V through the raw Q / dO tiles
+        b16_stage<T, HD>(rQ, b32_head<T>(p.k, b, hk), p.k.strides[2], k0, p.T, d, tid);
+        b16_stage<T, HD>(rO, b32_head<T>(p.v, b, hk), p.v.strides[2], k0, p.T, d, tid);
+        f32_cp_commit();
+        f32_cp_wait<0>();
+        __syncthreads();
+        b16_convert<T, HD>(sK, rQ, tid);
+        b16_convert<T, HD>(sV, rO, tid);
+        __syncthreads();
+    }
+    stage_q(sdO, rO, p.dout, 0);
     f32_cp_commit();
-    stage_q(sdO, p.dout, 0);
-    f32_cp_commit();
-    stage_q(sQ, p.q, 0);
+    stage_q(sQ, rQ, p.q, 0);
     f32_cp_commit();
 
     float dk[4][OC], dv[4][OC];
@@ -262,10 +401,25 @@ __global__ void __launch_bounds__(kB32Threads, 1) moda_bwd_f32_dkdv_kernel(const
         }
         f32_cp_wait<1>();  // this dO (this Q may still be in flight)
         __syncthreads();
+        if constexpr (!kIsF32<T>) {
+            b16_convert<T, HD>(sdO, rO, tid);
+            __syncthreads();
+            if (idx + 1 < nq) stage_q(sdO, rO, p.dout, idx + 1);
+            f32_cp_commit();
+        }
         float dpt[4][4];
         b32_abt<HD>(dpt, sV, sdO, ty, tx);
-        f32_cp_wait<0>();  // this Q
-        __syncthreads();
+        if constexpr (kIsF32<T>) {
+            f32_cp_wait<0>();  // this Q
+            __syncthreads();
+        } else {
+            f32_cp_wait<1>();  // this Q (the next dO may still be in flight)
+            __syncthreads();
+            b16_convert<T, HD>(sQ, rQ, tid);
+            __syncthreads();
+            if (idx + 1 < nq) stage_q(sQ, rQ, p.q, idx + 1);
+            f32_cp_commit();
+        }
         float st[4][4];
         b32_abt<HD>(st, sK, sQ, ty, tx);
         // queries before a key are masked: only the first token tile (tq0 == k0) has them,
@@ -284,17 +438,21 @@ __global__ void __launch_bounds__(kB32Threads, 1) moda_bwd_f32_dkdv_kernel(const
         }
         __syncthreads();
         b32_pm<HD>(dv, sP, sdO, ty, tx);
-        __syncthreads();  // every thread is done with dO and P
-        if (idx + 1 < nq) stage_q(sdO, p.dout, idx + 1);
-        f32_cp_commit();
+        if constexpr (kIsF32<T>) {
+            __syncthreads();  // every thread is done with dO and P
+            if (idx + 1 < nq) stage_q(sdO, rO, p.dout, idx + 1);
+            f32_cp_commit();
+        }
         b32_pm<HD>(dk, sdS, sQ, ty, tx);
-        __syncthreads();  // every thread is done with Q and dS
-        if (idx + 1 < nq) stage_q(sQ, p.q, idx + 1);
-        f32_cp_commit();
+        __syncthreads();  // every thread is done with Q, dO, P and dS
+        if constexpr (kIsF32<T>) {
+            if (idx + 1 < nq) stage_q(sQ, rQ, p.q, idx + 1);
+            f32_cp_commit();
+        }
     }
     f32_cp_wait<0>();
-    b32_store<HD>(p.dk, b, hk, k0, p.T, d, dk, p.scale, ty, tx);
-    b32_store<HD>(p.dv, b, hk, k0, p.T, d, dv, 1.f, ty, tx);
+    b32_store<T, HD>(p.dk, b, hk, k0, p.T, d, dk, p.scale, ty, tx);
+    b32_store<T, HD>(p.dv, b, hk, k0, p.T, d, dv, 1.f, ty, tx);
 }
 
 // Shared memory of the depth kernel, in floats: depth K and V rows [32][d+4], the token's
@@ -305,6 +463,7 @@ static int b32_depth_floats(int G, int d) {
     return 2 * kB32DepthRows * ds + 2 * G * ds + G * d + 2 * kB32DepthRows * gs + 2 * G;
 }
 
+template <typename T>
 __global__ void __launch_bounds__(kB32DepthThreads) moda_bwd_f32_depth_kernel(const __grid_constant__ BwdParams p) {
     extern __shared__ __align__(16) float b32_smem[];
     const int t = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
@@ -323,9 +482,10 @@ __global__ void __launch_bounds__(kB32DepthThreads) moda_bwd_f32_depth_kernel(co
 
     for (int i = tid; i < G * d4; i += kB32DepthThreads) {
         const int g = i / d4, c4 = i % d4, h = hk * G + g;
-        f32_cp16(sQ + g * ds + 4 * c4, b32_head(p.q, b, h) + static_cast<int64_t>(t) * p.q.strides[2] + 4 * c4, 16);
-        f32_cp16(sdO + g * ds + 4 * c4, b32_head(p.dout, b, h) + static_cast<int64_t>(t) * p.dout.strides[2] + 4 * c4,
-                 16);
+        b32_stage4<T>(sQ + g * ds + 4 * c4, b32_head<T>(p.q, b, h) + static_cast<int64_t>(t) * p.q.strides[2] + 4 * c4,
+                      true);
+        b32_stage4<T>(sdO + g * ds + 4 * c4,
+                      b32_head<T>(p.dout, b, h) + static_cast<int64_t>(t) * p.dout.strides[2] + 4 * c4, true);
     }
     f32_cp_commit();
     for (int i = tid; i < G * d; i += kB32DepthThreads) sDq[i] = 0.f;
@@ -334,10 +494,10 @@ __global__ void __launch_bounds__(kB32DepthThreads) moda_bwd_f32_depth_kernel(co
         sLse2[g] = p.lse[ri] * kLog2e;
         sDel[g] = p.delta[ri];
     }
-    const float* kdb = b32_head(p.kd, b, hk);
-    const float* vdb = b32_head(p.vd, b, hk);
-    float* dkdb = static_cast<float*>(p.dkd.ptr) + b * p.dkd.strides[0] + hk * p.dkd.strides[1];
-    float* dvdb = static_cast<float*>(p.dvd.ptr) + b * p.dvd.strides[0] + hk * p.dvd.strides[1];
+    const T* kdb = b32_head<T>(p.kd, b, hk);
+    const T* vdb = b32_head<T>(p.vd, b, hk);
+    T* dkdb = static_cast<T*>(p.dkd.ptr) + b * p.dkd.strides[0] + hk * p.dkd.strides[1];
+    T* dvdb = static_cast<T*>(p.dvd.ptr) + b * p.dvd.strides[0] + hk * p.dvd.strides[1];
     const int64_t r0 = static_cast<int64_t>(t) * p.L;
 
 #pragma unroll 1
@@ -347,8 +507,8 @@ __global__ void __launch_bounds__(kB32DepthThreads) moda_bwd_f32_depth_kernel(co
             const int r = i / d4, c4 = i % d4;
             const bool ok = r < nr;
             const int64_t row = r0 + l0 + r;
-            f32_cp16(sKd + r * ds + 4 * c4, ok ? kdb + row * p.kd.strides[2] + 4 * c4 : kdb, ok ? 16 : 0);
-            f32_cp16(sVd + r * ds + 4 * c4, ok ? vdb + row * p.vd.strides[2] + 4 * c4 : vdb, ok ? 16 : 0);
+            b32_stage4<T>(sKd + r * ds + 4 * c4, ok ? kdb + row * p.kd.strides[2] + 4 * c4 : kdb, ok);
+            b32_stage4<T>(sVd + r * ds + 4 * c4, ok ? vdb + row * p.vd.strides[2] + 4 * c4 : vdb, ok);
         }
         f32_cp_commit();
         f32_cp_wait<0>();
@@ -397,8 +557,8 @@ __global__ void __launch_bounds__(kB32DepthThreads) moda_bwd_f32_depth_kernel(co
                 dv4[3] = fmaf(pv, ov.w, dv4[3]);
             }
             const int64_t row = r0 + l0 + r;
-            f32_stv<4>(dkdb + row * p.dkd.strides[2] + 4 * c4, dk4, p.scale);
-            f32_stv<4>(dvdb + row * p.dvd.strides[2] + 4 * c4, dv4, 1.f);
+            b32_st4<T>(dkdb + row * p.dkd.strides[2] + 4 * c4, make_float4(dk4[0], dk4[1], dk4[2], dk4[3]), p.scale);
+            b32_st4<T>(dvdb + row * p.dvd.strides[2] + 4 * c4, make_float4(dv4[0], dv4[1], dv4[2], dv4[3]), 1.f);
         }
         // the depth part of dQ: sum over this chunk's rows of dS K_depth, by (head, 4 columns)
         for (int it = tid; it < G * d4; it += kB32DepthThreads) {
@@ -419,37 +579,39 @@ __global__ void __launch_bounds__(kB32DepthThreads) moda_bwd_f32_depth_kernel(co
     // dQ (the sequence part, from the dq kernel) += scale * the depth part
     for (int it = tid; it < G * d4; it += kB32DepthThreads) {
         const int g = it / d4, c4 = it % d4;
-        float* dqr = static_cast<float*>(p.dq.ptr) + b * p.dq.strides[0] + (hk * G + g) * p.dq.strides[1] +
+        T* dqr = static_cast<T*>(p.dq.ptr) + b * p.dq.strides[0] + (hk * G + g) * p.dq.strides[1] +
                      static_cast<int64_t>(t) * p.dq.strides[2] + 4 * c4;
-        float4 cur = *reinterpret_cast<float4*>(dqr);
+        float4 cur = b32_ld4<T>(dqr);
         const float4 a = *reinterpret_cast<const float4*>(sDq + g * d + 4 * c4);
         cur.x = fmaf(p.scale, a.x, cur.x);
         cur.y = fmaf(p.scale, a.y, cur.y);
         cur.z = fmaf(p.scale, a.z, cur.z);
         cur.w = fmaf(p.scale, a.w, cur.w);
-        *reinterpret_cast<float4*>(dqr) = cur;
+        b32_st4<T>(dqr, cur, 1.f);
     }
 }
 
 // depth rows [T*L, R) of dK_depth and dV_depth: never read by the forward, zero gradient
+template <typename T>
 __global__ void moda_bwd_f32_depth_zero_kernel(const __grid_constant__ BwdParams p) {
     const int hk = blockIdx.y, b = blockIdx.z;
     const int64_t first = static_cast<int64_t>(p.T) * p.L;
     const int64_t n = (p.R - first) * p.d;
-    float* dk = static_cast<float*>(p.dkd.ptr) + b * p.dkd.strides[0] + hk * p.dkd.strides[1];
-    float* dv = static_cast<float*>(p.dvd.ptr) + b * p.dvd.strides[0] + hk * p.dvd.strides[1];
+    T* dk = static_cast<T*>(p.dkd.ptr) + b * p.dkd.strides[0] + hk * p.dkd.strides[1];
+    T* dv = static_cast<T*>(p.dvd.ptr) + b * p.dvd.strides[0] + hk * p.dvd.strides[1];
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
         const int64_t r = first + i / p.d, c = i % p.d;
-        dk[r * p.dkd.strides[2] + c * p.dkd.strides[3]] = 0.f;
-        dv[r * p.dvd.strides[2] + c * p.dvd.strides[3]] = 0.f;
+        dk[r * p.dkd.strides[2] + c * p.dkd.strides[3]] = T{};
+        dv[r * p.dvd.strides[2] + c * p.dvd.strides[3]] = T{};
     }
 }
 
-// fp32 with d a multiple of 4 up to 128, G <= 32 and unit-stride, 16-byte aligned rows
-// (float4 copies) in every tensor the kernels read or write with vectors.
-bool f32_bwd_tiled_ok(const BwdParams& p) {
-    if (p.dtype != MODA_F32 || p.d % 4 != 0 || p.d > 128 || p.G > 32) return false;
+// fp32 or 16-bit with d a multiple of 4 up to 128, G <= 32 and unit-stride, 16-byte
+// aligned rows (16-byte copies) in every tensor the kernels read or write with vectors.
+bool bwd_tiled_ok(const BwdParams& p) {
+    const int esz = p.dtype == MODA_F32 ? 4 : (p.dtype == MODA_BF16 || p.dtype == MODA_F16) ? 2 : 0;
+    if (esz == 0 || p.d % 4 != 0 || p.d > 128 || p.G > 32) return false;
     if ((p.T + kB32Tile - 1) / kB32Tile > 65535 || static_cast<int64_t>(p.Hq) * p.B > INT32_MAX) return false;
     const ModaTensor* ts[11] = {&p.q, &p.k, &p.v, &p.dout, &p.dq, &p.dk, &p.dv, &p.kd, &p.vd, &p.dkd, &p.dvd};
     const int nts = p.L > 0 ? 11 : 7;
@@ -457,49 +619,61 @@ bool f32_bwd_tiled_ok(const BwdParams& p) {
         const ModaTensor* t = ts[i];
         if (t->strides[3] != 1 || reinterpret_cast<uintptr_t>(t->ptr) % 16 != 0) return false;
         for (int j = 0; j < 3; ++j)
-            if (t->sizes[j] > 1 && t->strides[j] % 4 != 0) return false;
+            if (t->sizes[j] > 1 && (t->strides[j] * esz) % 16 != 0) return false;
     }
     return true;
 }
 
-template <int HD>
+template <typename T, int HD>
 static int launch_b32_hd(const BwdParams& p, cudaStream_t stream) {
     using C = B32Cfg<HD>;
+    constexpr int raw = kIsF32<T> ? 0 : 2 * kB32Tile * HD * 2;  // two raw 16-bit tiles
+    constexpr int dq_bytes = C::kDqBytes + raw, dkv_bytes = C::kDkvBytes + raw;
     static std::atomic<uint64_t> dq_attr{0}, dkv_attr{0};
-    if (ensure_smem_attr(dq_attr, moda_bwd_f32_dq_kernel<HD>, C::kDqBytes) != cudaSuccess ||
-        ensure_smem_attr(dkv_attr, moda_bwd_f32_dkdv_kernel<HD>, C::kDkvBytes) != cudaSuccess)
+    if (ensure_smem_attr(dq_attr, moda_bwd_f32_dq_kernel<T, HD>, dq_bytes) != cudaSuccess ||
+        ensure_smem_attr(dkv_attr, moda_bwd_f32_dkdv_kernel<T, HD>, dkv_bytes) != cudaSuccess)
         return MODA_ERR_LAUNCH;
     const unsigned tiles = static_cast<unsigned>((p.T + kB32Tile - 1) / kB32Tile);
-    moda_bwd_f32_dq_kernel<HD><<<dim3(p.Hq * p.B, tiles), kB32Threads, C::kDqBytes, stream>>>(p);
-    moda_bwd_f32_dkdv_kernel<HD><<<dim3(p.Hk * p.B, tiles), kB32Threads, C::kDkvBytes, stream>>>(p);
+    moda_bwd_f32_dq_kernel<T, HD><<<dim3(p.Hq * p.B, tiles), kB32Threads, dq_bytes, stream>>>(p);
+    moda_bwd_f32_dkdv_kernel<T, HD><<<dim3(p.Hk * p.B, tiles), kB32Threads, dkv_bytes, stream>>>(p);
     return MODA_OK;
 }
 
 // dq, dkdv, then depth (which adds into dq) and the zero rows; rowsum(dO * O) is already
 // in p.delta.
-int launch_bwd_f32_tiled(const BwdParams& p, cudaStream_t stream) {
+template <typename T>
+static int launch_tiled_t(const BwdParams& p, cudaStream_t stream) {
     if (p.T > 0) {
-        const int r = p.d <= 32 ? launch_b32_hd<32>(p, stream)
-                      : p.d <= 64 ? launch_b32_hd<64>(p, stream)
-                                  : launch_b32_hd<128>(p, stream);
+        const int r = p.d <= 32 ? launch_b32_hd<T, 32>(p, stream)
+                      : p.d <= 64 ? launch_b32_hd<T, 64>(p, stream)
+                                  : launch_b32_hd<T, 128>(p, stream);
         if (r != MODA_OK) return r;
         if (p.L > 0) {
             static std::atomic<uint64_t> depth_attr{0};
             const int bytes = b32_depth_floats(p.G, p.d) * 4;
             // one opt-in at the largest size any G <= 32, d <= 128 needs
-            if (ensure_smem_attr(depth_attr, moda_bwd_f32_depth_kernel, b32_depth_floats(32, 128) * 4) !=
+            if (ensure_smem_attr(depth_attr, moda_bwd_f32_depth_kernel<T>, b32_depth_floats(32, 128) * 4) !=
                 cudaSuccess)
                 return MODA_ERR_LAUNCH;
-            moda_bwd_f32_depth_kernel<<<dim3(p.T, p.Hk, p.B), kB32DepthThreads, bytes, stream>>>(p);
+            moda_bwd_f32_depth_kernel<T><<<dim3(p.T, p.Hk, p.B), kB32DepthThreads, bytes, stream>>>(p);
         }
     }
     const int64_t extra = p.R - static_cast<int64_t>(p.T) * p.L;
     if (extra > 0) {
         const int64_t n = extra * p.d;
         const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, 1024));
-        moda_bwd_f32_depth_zero_kernel<<<dim3(blocks, p.Hk, p.B), 256, 0, stream>>>(p);
+        moda_bwd_f32_depth_zero_kernel<T><<<dim3(blocks, p.Hk, p.B), 256, 0, stream>>>(p);
     }
     return MODA_OK;
+}
+
+int launch_bwd_tiled(const BwdParams& p, cudaStream_t stream) {
+    switch (p.dtype) {
+        case MODA_F32: return launch_tiled_t<float>(p, stream);
+        case MODA_BF16: return launch_tiled_t<__nv_bfloat16>(p, stream);
+        case MODA_F16: return launch_tiled_t<__half>(p, stream);
+        default: return MODA_ERR_DTYPE;
+    }
 }
 
 }  // namespace moda

@@ -117,8 +117,8 @@ int launch_bwd(const BwdParams& p, cudaStream_t stream, char* err, size_t errlen
 bool tc_bwd_supports(const BwdParams& p, char* why, size_t whylen);
 int launch_bwd_tc(const BwdParams& p, cudaStream_t stream, char* err, size_t errlen);
 int launch_bwd_depth(const BwdParams& p, cudaStream_t stream);
-bool f32_bwd_tiled_ok(const BwdParams& p);
-int launch_bwd_f32_tiled(const BwdParams& p, cudaStream_t stream);
+bool bwd_tiled_ok(const BwdParams& p);
+int launch_bwd_tiled(const BwdParams& p, cudaStream_t stream);
 cudaError_t read_and_clear_bwd_status(cudaStream_t stream, int* value);
 constexpr int kMaxDevices = 64;
 // Device address of the library's fixed backward scratch on the current device.

@@ -1,7 +1,9 @@
-"""The fp32 backward in CUDA-core tiles (csrc/moda_bwd_f32.cu) against the oracle.
+"""The backward in CUDA-core tiles (csrc/moda_bwd_f32.cu) against the oracle.
 
 fp32 inputs with d a multiple of 4 up to 128, G <= 32 and 16-byte aligned rows take the
-tiled kernels; other fp32 layouts take the row kernels (csrc/moda_bwd.cu). Both are
+tiled kernels, and so do bf16 / f16 inputs of the shapes the tensor-core backward does
+not take (head_dim outside {64, 128}, H_q / H_k not dividing 128); other layouts take
+the row kernels (csrc/moda_bwd.cu). Both are
 checked here: shapes across the tile edges (T around 64, head_dim 8 / 36 / 96 / 128, L
 over one 32-row depth chunk, G = 1 .. 32, extra depth rows past T*L), the row-kernel
 route through misaligned views, and at a medium size (B=1, H_q=32, H_k=8, T=2048,
@@ -9,7 +11,8 @@ d=128, L=32) the exact per-token gradients of sampled tokens plus two identities
 full gradients per KV head: sum of dV over all key rows (sequence and depth) equals sum
 of dO over the head group's query rows (each softmax row sums to one), and the sum of
 dK over all key rows is zero (each row of dS sums to zero).
-Tolerance: max|g - ref| / max|ref| <= 1e-4 for every gradient (FP32_REL_TOL).
+Tolerance: max|g - ref| / max|ref| <= 1e-4 for every gradient (FP32_REL_TOL); 16-bit
+inputs against the fp64 oracle on the same rounded inputs: 3e-2 of max(1, max|ref|).
 """
 
 import numpy as np
@@ -133,3 +136,31 @@ def test_fp32_medium_shape_tokens_and_identities():
     assert np.max(np.abs(sum_dv - sum_do)) <= 1e-4 * np.max(np.abs(sum_do)) + 1e-3
     sum_dk = h(dK.sum(2)) + h(dKd.sum(2))
     assert np.max(np.abs(sum_dk)) <= 1e-4 * float(h(dK.abs().sum(2)).max())
+
+
+# 16-bit shapes the tensor-core backward does not take: (B, H_q, H_k, T, d, L, extra)
+HALF_CASES = [
+    (1, 6, 2, 70, 64, 3, 0),      # G = 3
+    (1, 10, 2, 129, 128, 5, 0),   # G = 5, head_dim 128
+    (2, 4, 2, 65, 32, 4, 0),      # head_dim 32
+    (1, 6, 2, 100, 96, 33, 9),    # head_dim 96, G = 3, two depth chunks, extra depth rows
+    (1, 4, 4, 50, 36, 2, 0),      # head_dim 36 (a partial 8-element copy per row)
+]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "f16"])
+@pytest.mark.parametrize("case", HALF_CASES, ids=["-".join(map(str, c)) for c in HALF_CASES])
+def test_half_grads_in_tiles_match_oracle(case, dtype):
+    B, Hq, Hk, T, d, L, extra = case
+    arrs = seeded_inputs(B, Hq, Hk, T, d, L, seed=500 + T + d, extra_rows=extra)
+    args = [torch.from_numpy(np.ascontiguousarray(a)).to("cuda", dtype) for a in arrs]
+    rin = [t.double().cpu().numpy() for t in args]
+    dO = torch.from_numpy(np.random.default_rng(T + d).standard_normal((B, Hq, T, d))).to("cuda", dtype)
+    got = _grads(args, L, dO)
+    ref = orc.moda_attention_grads(*rin, L, dO.double().cpu().numpy())
+    for k, g in zip(GRADS, got):
+        assert g.shape == ref[k].shape, k
+        e = float(np.abs(g - ref[k]).max()) / max(1.0, float(np.abs(ref[k]).max()))
+        assert e <= 3e-2, (k, e)
+    if extra:
+        assert not np.any(got[3][:, :, T * L:]) and not np.any(got[4][:, :, T * L:])
