@@ -52,8 +52,10 @@ def test_plan_by_dtype_and_head_dim(d, dtype, expect):
     assert _plan(1, 8, 2, 100, d, 4, dtype) == expect
 
 
+# groups that do not divide 128 (3, 6, 12) run the tensor-core kernel as G launches with
+# one query head per KV head; above 128 heads per group, the CUDA-core kernel
 @pytest.mark.parametrize("G,expect", [(1, "tc"), (2, "tc"), (4, "tc"), (8, "tc"), (16, "tc"),
-                                      (3, "simt"), (6, "simt")])
+                                      (3, "tc"), (6, "tc"), (12, "tc"), (160, "simt")])
 def test_plan_by_group_size(G, expect):
     assert _plan(1, 2 * G, 2, 64, 128, 2) == expect
 
