@@ -53,7 +53,8 @@ its own ``moda_attention_naive`` (chunked; ``baseline/_ref``, unmodified), same 
 
 ``--dtype fp32`` runs ``--pass backward``, ``triton-reference`` or ``reference-train`` on
 fp32 inputs (this library's CUDA-core kernels); ``--batch`` and ``--seq`` shrink B and T
-for those passes.
+for those passes, ``--heads HQ,HK`` sets the head counts (for example 24,8: three query
+heads per KV head) and ``--head-dim`` the head dimension.
 
 ``--pass backward`` (one GPU) times the backward kernels instead: one step = the
 gradients of all five inputs for a seeded dO, from the forward's O and row
@@ -458,6 +459,10 @@ def main():
                     help="batch override for --pass proj / backward / triton-reference / reference-train")
     ap.add_argument("--seq", type=int, default=None,
                     help="sequence-length override for --pass backward / triton-reference / reference-train")
+    ap.add_argument("--head-dim", type=int, default=None,
+                    help="head_dim for --pass backward / triton-reference / reference-train")
+    ap.add_argument("--heads", default=None, metavar="HQ,HK",
+                    help="query and KV head counts for --pass backward / triton-reference / reference-train")
     ap.add_argument("--dtype", choices=["bf16", "fp32"], default="bf16",
                     help="input dtype for --pass backward / triton-reference / reference-train")
     ap.add_argument("--graph", action="store_true",
@@ -469,10 +474,18 @@ def main():
     side = ("backward", "triton-reference", "reference-train")
     if args.which in side:
         wl = resized(wl, args.batch, args.seq)
+        if args.heads:
+            hq, hk = (int(x) for x in args.heads.split(","))
+            if hq <= 0 or hk <= 0 or hq % hk:
+                ap.error("--heads needs HQ,HK with HK dividing HQ")
+            wl = dict(wl, Hq=hq, Hk=hk, desc=wl["desc"].replace(f"H_q={wl['Hq']} H_k={wl['Hk']}",
+                                                                  f"H_q={hq} H_k={hk}"))
+        if args.head_dim:
+            wl = dict(wl, d=args.head_dim, desc=wl["desc"].replace(f"d={wl['d']} ", f"d={args.head_dim} "))
         if args.dtype == "fp32":
             wl = dict(wl, desc=wl["desc"].replace("bf16 fp32-accumulate", "fp32").replace("bf16", "fp32"))
-    elif args.dtype != "bf16" or args.seq is not None:
-        ap.error("--dtype and --seq apply to --pass " + " / ".join(side))
+    elif args.dtype != "bf16" or args.seq is not None or args.heads is not None or args.head_dim is not None:
+        ap.error("--dtype, --seq, --heads and --head-dim apply to --pass " + " / ".join(side))
     if args.impl == "reference":
         return run_reference(args, wl)
     if args.which == "backward":

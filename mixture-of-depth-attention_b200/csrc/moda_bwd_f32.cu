@@ -48,46 +48,6 @@ struct B32Cfg {
 
 namespace {
 
-template <typename T>
-constexpr bool kIsF32 = std::is_same<T, float>::value;
-
-template <typename T>
-MODA_DEV float2 unpack2(uint32_t w);  // two 16-bit values, low half first
-template <>
-MODA_DEV float2 unpack2<__nv_bfloat16>(uint32_t w) {
-    return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
-}
-template <>
-MODA_DEV float2 unpack2<__half>(uint32_t w) {
-    return make_float2(__half2float(__ushort_as_half(static_cast<unsigned short>(w & 0xffffu))),
-                       __half2float(__ushort_as_half(static_cast<unsigned short>(w >> 16))));
-}
-template <typename T>
-MODA_DEV uint32_t pack2(float lo, float hi);
-template <>
-MODA_DEV uint32_t pack2<__nv_bfloat16>(float lo, float hi) { return pack_bf16x2(lo, hi); }
-template <>
-MODA_DEV uint32_t pack2<__half>(float lo, float hi) { return pack_f16x2(lo, hi); }
-
-// 4 consecutive elements as floats / from floats times s (16-bit: one 8-byte access)
-template <typename T>
-MODA_DEV float4 b32_ld4(const T* src) {
-    if constexpr (kIsF32<T>) {
-        return *reinterpret_cast<const float4*>(src);
-    } else {
-        const uint2 w = *reinterpret_cast<const uint2*>(src);
-        const float2 a = unpack2<T>(w.x), c = unpack2<T>(w.y);
-        return make_float4(a.x, a.y, c.x, c.y);
-    }
-}
-template <typename T>
-MODA_DEV void b32_st4(T* dst, float4 v, float s) {
-    if constexpr (kIsF32<T>)
-        *reinterpret_cast<float4*>(dst) = make_float4(v.x * s, v.y * s, v.z * s, v.w * s);
-    else
-        *reinterpret_cast<uint2*>(dst) = make_uint2(pack2<T>(v.x * s, v.y * s), pack2<T>(v.z * s, v.w * s));
-}
-
 // 4 elements into 4 floats of shared memory (zeros when !ok): fp32 by cp.async, 16-bit
 // by one 8-byte load and a conversion
 template <typename T>
@@ -99,29 +59,14 @@ MODA_DEV void b32_stage4(float* dst, const T* src, bool ok) {
     }
 }
 
-// 64 rows of a [.., rows, d] 16-bit view, from row0, into a raw [64][HD] tile by cp.async
-// (16 bytes = 8 elements per copy; zeros for rows at or past `limit` and columns at or
-// past d)
+// raw 16-bit tiles of this file's 64 rows with its 256 threads
 template <typename T, int HD>
 MODA_DEV void b16_stage(T* dst, const T* base, int64_t rstride, int row0, int limit, int d, int tid) {
-    for (int i = tid; i < kB32Tile * (HD / 8); i += kB32Threads) {
-        const int r = i / (HD / 8), col = 8 * (i % (HD / 8));
-        const int n = row0 + r < limit && col < d ? min(8, d - col) : 0;  // elements to copy
-        const T* src = n ? base + static_cast<int64_t>(row0 + r) * rstride + col : base;
-        f32_cp16(reinterpret_cast<float*>(dst + r * HD + col), reinterpret_cast<const float*>(src), 2 * n);
-    }
+    raw16_stage<T, HD, kB32Tile, kB32Threads>(dst, base, rstride, row0, limit, d, tid);
 }
-
-// raw [64][HD] 16-bit tile -> fp32 [64][HD+4] tile
 template <typename T, int HD>
 MODA_DEV void b16_convert(float* dst, const T* raw, int tid) {
-    for (int i = tid; i < kB32Tile * (HD / 8); i += kB32Threads) {
-        const int r = i / (HD / 8), col = 8 * (i % (HD / 8));
-        const uint4 w = *reinterpret_cast<const uint4*>(raw + r * HD + col);
-        const float2 a = unpack2<T>(w.x), b = unpack2<T>(w.y), c = unpack2<T>(w.z), e = unpack2<T>(w.w);
-        *reinterpret_cast<float4*>(dst + r * (HD + 4) + col) = make_float4(a.x, a.y, b.x, b.y);
-        *reinterpret_cast<float4*>(dst + r * (HD + 4) + col + 4) = make_float4(c.x, c.y, e.x, e.y);
-    }
+    raw16_convert<T, HD, kB32Tile, kB32Threads>(dst, raw, tid);
 }
 
 // 64 rows of a [.., rows, d] fp32 view, from row0, into dst [64][HD+4] by cp.async

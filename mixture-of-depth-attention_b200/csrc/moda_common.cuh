@@ -13,6 +13,8 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <type_traits>
+
 namespace moda {
 
 // Error word written by kernels (0 = fine): 0x100 | site for a wait that timed
@@ -339,6 +341,95 @@ MODA_DEV void f32_stv(float* dst, const float* src, float s) {
         *reinterpret_cast<float4*>(dst) = make_float4(src[0] * s, src[1] * s, src[2] * s, src[3] * s);
     else
         *reinterpret_cast<float2*>(dst) = make_float2(src[0] * s, src[1] * s);
+}
+
+// ------------------------------------------------------------------ fp32 / 16-bit values
+template <typename T>
+constexpr bool kIsF32 = std::is_same<T, float>::value;
+
+template <typename T>
+MODA_DEV float2 unpack2(uint32_t w);  // two 16-bit values, low half first
+template <>
+MODA_DEV float2 unpack2<__nv_bfloat16>(uint32_t w) {
+    return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+template <>
+MODA_DEV float2 unpack2<__half>(uint32_t w) {
+    return make_float2(__half2float(__ushort_as_half(static_cast<unsigned short>(w & 0xffffu))),
+                       __half2float(__ushort_as_half(static_cast<unsigned short>(w >> 16))));
+}
+template <typename T>
+MODA_DEV uint32_t pack2(float lo, float hi);
+template <>
+MODA_DEV uint32_t pack2<__nv_bfloat16>(float lo, float hi) { return pack_bf16x2(lo, hi); }
+template <>
+MODA_DEV uint32_t pack2<__half>(float lo, float hi) { return pack_f16x2(lo, hi); }
+
+// 4 consecutive elements as floats / from floats times s (16-bit: one 8-byte access)
+template <typename T>
+MODA_DEV float4 b32_ld4(const T* src) {
+    if constexpr (kIsF32<T>) {
+        return *reinterpret_cast<const float4*>(src);
+    } else {
+        const uint2 w = *reinterpret_cast<const uint2*>(src);
+        const float2 a = unpack2<T>(w.x), c = unpack2<T>(w.y);
+        return make_float4(a.x, a.y, c.x, c.y);
+    }
+}
+template <typename T>
+MODA_DEV void b32_st4(T* dst, float4 v, float s) {
+    if constexpr (kIsF32<T>)
+        *reinterpret_cast<float4*>(dst) = make_float4(v.x * s, v.y * s, v.z * s, v.w * s);
+    else
+        *reinterpret_cast<uint2*>(dst) = make_uint2(pack2<T>(v.x * s, v.y * s), pack2<T>(v.z * s, v.w * s));
+}
+
+// ROWS rows of a [.., rows, d] 16-bit view, from row0, into a raw [ROWS][HD] tile by
+// cp.async, NT threads (16 bytes = 8 elements per copy; zeros for rows at or past
+// `limit` and for columns at or past d, which must be a multiple of 4)
+template <typename T, int HD, int ROWS, int NT>
+MODA_DEV void raw16_stage(T* dst, const T* base, int64_t rstride, int row0, int limit, int d, int tid) {
+    for (int i = tid; i < ROWS * (HD / 8); i += NT) {
+        const int r = i / (HD / 8), col = 8 * (i % (HD / 8));
+        const int n = row0 + r < limit && col < d ? min(8, d - col) : 0;  // elements to copy
+        const T* src = n ? base + static_cast<int64_t>(row0 + r) * rstride + col : base;
+        f32_cp16(reinterpret_cast<float*>(dst + r * HD + col), reinterpret_cast<const float*>(src), 2 * n);
+    }
+}
+
+// raw [ROWS][HD] 16-bit tile -> fp32 [ROWS][HD+4] tile, NT threads
+template <typename T, int HD, int ROWS, int NT>
+MODA_DEV void raw16_convert(float* dst, const T* raw, int tid) {
+    for (int i = tid; i < ROWS * (HD / 8); i += NT) {
+        const int r = i / (HD / 8), col = 8 * (i % (HD / 8));
+        const uint4 w = *reinterpret_cast<const uint4*>(raw + r * HD + col);
+        const float2 a = unpack2<T>(w.x), b = unpack2<T>(w.y), c = unpack2<T>(w.z), e = unpack2<T>(w.w);
+        *reinterpret_cast<float4*>(dst + r * (HD + 4) + col) = make_float4(a.x, a.y, b.x, b.y);
+        *reinterpret_cast<float4*>(dst + r * (HD + 4) + col + 4) = make_float4(c.x, c.y, e.x, e.y);
+    }
+}
+
+// W consecutive elements (W = 2 or 4) as floats / from floats times s, one access
+template <typename T, int W>
+MODA_DEV void ldv_as_f32(float* dst, const T* src) {
+    if constexpr (kIsF32<T>) {
+        f32_ldv<W>(dst, src);
+    } else if constexpr (W == 4) {
+        const float4 v = b32_ld4<T>(src);
+        dst[0] = v.x, dst[1] = v.y, dst[2] = v.z, dst[3] = v.w;
+    } else {
+        const float2 v = unpack2<T>(*reinterpret_cast<const uint32_t*>(src));
+        dst[0] = v.x, dst[1] = v.y;
+    }
+}
+template <typename T, int W>
+MODA_DEV void stv_from_f32(T* dst, const float* src, float s) {
+    if constexpr (kIsF32<T>)
+        f32_stv<W>(dst, src, s);
+    else if constexpr (W == 4)
+        b32_st4<T>(dst, make_float4(src[0], src[1], src[2], src[3]), s);
+    else
+        *reinterpret_cast<uint32_t*>(dst) = pack2<T>(src[0] * s, src[1] * s);
 }
 
 // ------------------------------------------------------------------ UMMA descriptors

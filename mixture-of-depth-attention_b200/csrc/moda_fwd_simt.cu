@@ -153,7 +153,7 @@ struct F32Cfg {
     static constexpr int kBytes = kFloats * 4;
 };
 
-template <int HD, int RPT>
+template <typename T, int HD, int RPT>
 __global__ void __launch_bounds__(f32_threads(RPT), 1) moda_fwd_f32_tiled_kernel(const FwdParams p) {
     using C = F32Cfg<HD>;
     // RPT query rows per thread, RS apart (RS = 128 / RPT threads per key column)
@@ -168,6 +168,8 @@ __global__ void __launch_bounds__(f32_threads(RPT), 1) moda_fwd_f32_tiled_kernel
     float* sK = f32_smem + C::kK;
     float* sV = f32_smem + C::kV;
     float* sP = f32_smem + C::kP;
+    T* rK = reinterpret_cast<T*>(f32_smem + C::kFloats);  // 16-bit only: raw K and V tiles
+    T* rV = rK + kF32Keys * HD;
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
     const int ntiles = (p.T + kF32Rows - 1) / kF32Rows;
     // grid (H_q * B, tiles): dispatch runs x fastest, so every head's heaviest tile (the
@@ -175,12 +177,13 @@ __global__ void __launch_bounds__(f32_threads(RPT), 1) moda_fwd_f32_tiled_kernel
     const int t0 = (ntiles - 1 - static_cast<int>(blockIdx.y)) * kF32Rows;
     const int h = blockIdx.x % p.Hq, b = blockIdx.x / p.Hq, hk = h / p.G;
     const int d = p.d;
-    const float* qb = static_cast<const float*>(p.q.ptr) + b * p.q.strides[0] + h * p.q.strides[1];
-    const float* kb = static_cast<const float*>(p.k.ptr) + b * p.k.strides[0] + hk * p.k.strides[1];
-    const float* vb = static_cast<const float*>(p.v.ptr) + b * p.v.strides[0] + hk * p.v.strides[1];
+    const T* qb = static_cast<const T*>(p.q.ptr) + b * p.q.strides[0] + h * p.q.strides[1];
+    const T* kb = static_cast<const T*>(p.k.ptr) + b * p.k.strides[0] + hk * p.k.strides[1];
+    const T* vb = static_cast<const T*>(p.v.ptr) + b * p.v.strides[0] + hk * p.v.strides[1];
     const float sc = p.scale * kLog2e;
 
-    // stage `rows` rows starting at row0 of a [.., rows, d] view into dst (zeros past T or d)
+    // fp32: stage `rows` rows starting at row0 of a [.., rows, d] view into dst (zeros
+    // past T or d); 16-bit rows go through the raw tiles (raw16_stage, raw16_convert)
     auto stage = [&](float* dst, const float* base, int64_t rstride, int row0, int rows, int limit) {
         for (int i = tid; i < rows * (HD / 4); i += NT) {
             const int r = i / (HD / 4), c4 = i % (HD / 4);
@@ -191,12 +194,27 @@ __global__ void __launch_bounds__(f32_threads(RPT), 1) moda_fwd_f32_tiled_kernel
     };
     const int kmax = min(t0 + kF32Rows, p.T);           // keys [0, kmax) are needed
     const int nkt = (kmax + kF32Keys - 1) / kF32Keys;    // causal key tiles
-    stage(sQ, qb, p.q.strides[2], t0, kF32Rows, p.T);
-    f32_cp_commit();
-    stage(sK, kb, p.k.strides[2], 0, kF32Keys, p.T);
-    f32_cp_commit();
-    stage(sV, vb, p.v.strides[2], 0, kF32Keys, p.T);
-    f32_cp_commit();
+    if constexpr (kIsF32<T>) {
+        stage(sQ, qb, p.q.strides[2], t0, kF32Rows, p.T);
+        f32_cp_commit();
+        stage(sK, kb, p.k.strides[2], 0, kF32Keys, p.T);
+        f32_cp_commit();
+        stage(sV, vb, p.v.strides[2], 0, kF32Keys, p.T);
+        f32_cp_commit();
+    } else {  // Q in two 64-row halves through the raw K / V tiles, then the first K and V
+        raw16_stage<T, HD, kF32Keys, NT>(rK, qb, p.q.strides[2], t0, p.T, d, tid);
+        raw16_stage<T, HD, kF32Keys, NT>(rV, qb, p.q.strides[2], t0 + kF32Keys, p.T, d, tid);
+        f32_cp_commit();
+        f32_cp_wait<0>();
+        __syncthreads();
+        raw16_convert<T, HD, kF32Keys, NT>(sQ, rK, tid);
+        raw16_convert<T, HD, kF32Keys, NT>(sQ + kF32Keys * C::kStride, rV, tid);
+        __syncthreads();
+        raw16_stage<T, HD, kF32Keys, NT>(rK, kb, p.k.strides[2], 0, p.T, d, tid);
+        f32_cp_commit();
+        raw16_stage<T, HD, kF32Keys, NT>(rV, vb, p.v.strides[2], 0, p.T, d, tid);
+        f32_cp_commit();
+    }
 
     float o[RPT][OC], m[RPT], l[RPT];
 #pragma unroll
@@ -211,8 +229,8 @@ __global__ void __launch_bounds__(f32_threads(RPT), 1) moda_fwd_f32_tiled_kernel
 
     // ---- 1. depth rows: row ty + RS*i is token t0 + ty + RS*i; its 16 threads split the L rows
     if (p.L > 0) {
-        const float* kdb = static_cast<const float*>(p.kd.ptr) + b * p.kd.strides[0] + hk * p.kd.strides[1];
-        const float* vdb = static_cast<const float*>(p.vd.ptr) + b * p.vd.strides[0] + hk * p.vd.strides[1];
+        const T* kdb = static_cast<const T*>(p.kd.ptr) + b * p.kd.strides[0] + hk * p.kd.strides[1];
+        const T* vdb = static_cast<const T*>(p.vd.ptr) + b * p.vd.strides[0] + hk * p.vd.strides[1];
 #pragma unroll
         for (int i = 0; i < RPT; ++i) {  // unrolled: o, m and l stay in registers
             const int r = ty + RS * i, t = t0 + r;
@@ -240,10 +258,10 @@ __global__ void __launch_bounds__(f32_threads(RPT), 1) moda_fwd_f32_tiled_kernel
 #pragma unroll
                     for (int uu = 0; uu < 8; ++uu) {
                         const bool okr = u0 + uu < nrows;  // the same for the whole warp
-                        const float* kr = kdb + (row0 + l0 + (okr ? u0 + uu : 0)) * p.kd.strides[2] + tx * VW;
+                        const T* kr = kdb + (row0 + l0 + (okr ? u0 + uu : 0)) * p.kd.strides[2] + tx * VW;
 #pragma unroll
                         for (int g = 0; g < NG; ++g) {
-                            if (okr && tx * VW + g * 16 * VW < d) f32_ldv<VW>(kv[uu] + g * VW, kr + g * 16 * VW);
+                            if (okr && tx * VW + g * 16 * VW < d) ldv_as_f32<T, VW>(kv[uu] + g * VW, kr + g * 16 * VW);
                             else
 #pragma unroll
                                 for (int w = 0; w < VW; ++w) kv[uu][g * VW + w] = 0.f;
@@ -284,10 +302,10 @@ __global__ void __launch_bounds__(f32_threads(RPT), 1) moda_fwd_f32_tiled_kernel
 #pragma unroll
                     for (int uu = 0; uu < 8; ++uu) {
                         const bool okr = valid && u0 + uu < nrows;
-                        const float* vr = vdb + (row0 + l0 + (okr ? u0 + uu : 0)) * p.vd.strides[2] + tx * VW;
+                        const T* vr = vdb + (row0 + l0 + (okr ? u0 + uu : 0)) * p.vd.strides[2] + tx * VW;
 #pragma unroll
                         for (int g = 0; g < NG; ++g) {
-                            if (okr && tx * VW + g * 16 * VW < d) f32_ldv<VW>(vv[uu] + g * VW, vr + g * 16 * VW);
+                            if (okr && tx * VW + g * 16 * VW < d) ldv_as_f32<T, VW>(vv[uu] + g * VW, vr + g * 16 * VW);
                             else
 #pragma unroll
                                 for (int w = 0; w < VW; ++w) vv[uu][g * VW + w] = 0.f;
@@ -312,6 +330,12 @@ __global__ void __launch_bounds__(f32_threads(RPT), 1) moda_fwd_f32_tiled_kernel
     for (int kt = 0; kt < nkt; ++kt) {
         f32_cp_wait<1>();  // this tile's K (its V may still be in flight)
         __syncthreads();
+        if constexpr (!kIsF32<T>) {
+            raw16_convert<T, HD, kF32Keys, NT>(sK, rK, tid);
+            __syncthreads();
+            if (kt + 1 < nkt) raw16_stage<T, HD, kF32Keys, NT>(rK, kb, p.k.strides[2], (kt + 1) * kF32Keys, p.T, d, tid);
+            f32_cp_commit();
+        }
         float s[RPT][4];
 #pragma unroll
         for (int i = 0; i < RPT; ++i)
@@ -334,9 +358,11 @@ __global__ void __launch_bounds__(f32_threads(RPT), 1) moda_fwd_f32_tiled_kernel
                     s[i][j] = fmaf(qv[i].w, kv[j].w, s[i][j]);
                 }
         }
-        __syncthreads();  // every thread is done with this K tile
-        if (kt + 1 < nkt) stage(sK, kb, p.k.strides[2], (kt + 1) * kF32Keys, kF32Keys, p.T);
-        f32_cp_commit();
+        if constexpr (kIsF32<T>) {
+            __syncthreads();  // every thread is done with this K tile
+            if (kt + 1 < nkt) stage(sK, kb, p.k.strides[2], (kt + 1) * kF32Keys, kF32Keys, p.T);
+            f32_cp_commit();
+        }
         // online softmax over this tile; keys after the row's token are masked
         const bool diag = kt * kF32Keys + kF32Keys - 1 > t0;
 #pragma unroll
@@ -368,6 +394,12 @@ __global__ void __launch_bounds__(f32_threads(RPT), 1) moda_fwd_f32_tiled_kernel
         }
         f32_cp_wait<1>();  // this tile's V (the next K may still be in flight)
         __syncthreads();   // and P from every thread
+        if constexpr (!kIsF32<T>) {
+            raw16_convert<T, HD, kF32Keys, NT>(sV, rV, tid);
+            __syncthreads();
+            if (kt + 1 < nkt) raw16_stage<T, HD, kF32Keys, NT>(rV, vb, p.v.strides[2], (kt + 1) * kF32Keys, p.T, d, tid);
+            f32_cp_commit();
+        }
 #pragma unroll 2
         for (int k = 0; k < kF32Keys; k += 4) {
             float4 pv[RPT];
@@ -387,14 +419,16 @@ __global__ void __launch_bounds__(f32_threads(RPT), 1) moda_fwd_f32_tiled_kernel
                 }
             }
         }
-        __syncthreads();  // every thread is done with this V tile and with P
-        if (kt + 1 < nkt) stage(sV, vb, p.v.strides[2], (kt + 1) * kF32Keys, kF32Keys, p.T);
-        f32_cp_commit();
+        if constexpr (kIsF32<T>) {
+            __syncthreads();  // every thread is done with this V tile and with P
+            if (kt + 1 < nkt) stage(sV, vb, p.v.strides[2], (kt + 1) * kF32Keys, kF32Keys, p.T);
+            f32_cp_commit();
+        }  // 16-bit: the next tile's first barrier orders its K conversion after this P V
     }
     f32_cp_wait<0>();
 
     // ---- epilogue: O / l, the zero_rows keys, the log-sum-exp
-    float* obase = static_cast<float*>(p.o.ptr) + b * p.o.strides[0] + h * p.o.strides[1];
+    T* obase = static_cast<T*>(p.o.ptr) + b * p.o.strides[0] + h * p.o.strides[1];
 #pragma unroll
     for (int i = 0; i < RPT; ++i) {
         float lt = l[i];
@@ -411,17 +445,19 @@ __global__ void __launch_bounds__(f32_threads(RPT), 1) moda_fwd_f32_tiled_kernel
         const float inv = a / lt;
         if (p.lse && tx == 0)  // natural log of sum_j exp(scale * q.k_j)
             p.lse[(static_cast<int64_t>(b) * p.Hq + h) * p.T + t] = (mf + __log2f(lt)) * kLn2;
-        float* orow = obase + static_cast<int64_t>(t) * p.o.strides[2] + tx * VW;
+        T* orow = obase + static_cast<int64_t>(t) * p.o.strides[2] + tx * VW;
 #pragma unroll
         for (int g = 0; g < NG; ++g)
-            if (tx * VW + g * 16 * VW < d) f32_stv<VW>(orow + g * 16 * VW, o[i] + g * VW, inv);
+            if (tx * VW + g * 16 * VW < d) stv_from_f32<T, VW>(orow + g * 16 * VW, o[i] + g * VW, inv);
     }
 }
 
-// The tiled fp32 kernel serves d a multiple of 4 up to 128 with unit-stride, 16-byte
-// aligned rows (float4 copies); everything else takes the row kernel.
-static bool f32_tiled_ok(const FwdParams& p) {
-    if (p.dtype != MODA_F32 || p.d % 4 != 0 || p.d > 128) return false;
+// The tiled kernel serves fp32, and bf16 / f16 that the tensor-core kernel does not take,
+// with d a multiple of 4 up to 128 and unit-stride, 16-byte aligned rows (16-byte
+// copies); everything else takes the row kernel.
+static bool tiled_ok(const FwdParams& p) {
+    const int esz = p.dtype == MODA_F32 ? 4 : (p.dtype == MODA_BF16 || p.dtype == MODA_F16) ? 2 : 0;
+    if (esz == 0 || p.d % 4 != 0 || p.d > 128) return false;
     if ((p.T + kF32Rows - 1) / kF32Rows > 65535 || static_cast<int64_t>(p.Hq) * p.B > INT32_MAX) return false;
     const ModaTensor* ts[6] = {&p.q, &p.k, &p.v, &p.o, &p.kd, &p.vd};
     const int nts = p.L > 0 ? 6 : 4;
@@ -429,28 +465,36 @@ static bool f32_tiled_ok(const FwdParams& p) {
         const ModaTensor* t = ts[i];
         if (t->strides[3] != 1 || reinterpret_cast<uintptr_t>(t->ptr) % 16 != 0) return false;
         for (int j = 0; j < 3; ++j)
-            if (t->sizes[j] > 1 && t->strides[j] % 4 != 0) return false;
+            if (t->sizes[j] > 1 && (t->strides[j] * esz) % 16 != 0) return false;
     }
     return true;
 }
 
-template <int HD>
-static int launch_f32_tiled_hd(const FwdParams& p, cudaStream_t stream) {
+template <typename T, int HD>
+static int launch_tiled_hd(const FwdParams& p, cudaStream_t stream) {
     using C = F32Cfg<HD>;
     static std::atomic<uint64_t> attr_done{0};
     constexpr int RPT = kF32RowsPerThread;
-    if (ensure_smem_attr(attr_done, moda_fwd_f32_tiled_kernel<HD, RPT>, C::kBytes) != cudaSuccess)
+    constexpr int bytes = C::kBytes + (kIsF32<T> ? 0 : 2 * kF32Keys * HD * 2);  // + raw K, V tiles
+    if (ensure_smem_attr(attr_done, moda_fwd_f32_tiled_kernel<T, HD, RPT>, bytes) != cudaSuccess)
         return MODA_ERR_LAUNCH;
     const dim3 grid(p.Hq * p.B, (p.T + kF32Rows - 1) / kF32Rows);
-    moda_fwd_f32_tiled_kernel<HD, RPT><<<grid, f32_threads(RPT), C::kBytes, stream>>>(p);
+    moda_fwd_f32_tiled_kernel<T, HD, RPT><<<grid, f32_threads(RPT), bytes, stream>>>(p);
     return MODA_OK;
 }
 
+template <typename T>
+static int launch_tiled_t(const FwdParams& p, cudaStream_t stream) {
+    if (p.d <= 32) return launch_tiled_hd<T, 32>(p, stream);
+    if (p.d <= 64) return launch_tiled_hd<T, 64>(p, stream);
+    return launch_tiled_hd<T, 128>(p, stream);
+}
+
 int launch_fwd_simt(const FwdParams& p, cudaStream_t stream) {
-    if (f32_tiled_ok(p)) {
-        if (p.d <= 32) return launch_f32_tiled_hd<32>(p, stream);
-        if (p.d <= 64) return launch_f32_tiled_hd<64>(p, stream);
-        return launch_f32_tiled_hd<128>(p, stream);
+    if (tiled_ok(p)) {
+        if (p.dtype == MODA_F32) return launch_tiled_t<float>(p, stream);
+        if (p.dtype == MODA_BF16) return launch_tiled_t<__nv_bfloat16>(p, stream);
+        return launch_tiled_t<__half>(p, stream);
     }
     const dim3 grid((p.T + kSimtRows - 1) / kSimtRows, p.Hq, p.B);
     const dim3 block(kSimtRows * 32);

@@ -389,3 +389,21 @@ def test_tc_odd_group_gradients_match_oracle():
     for t, k in zip(ins, ("dQ", "dK", "dV", "dK_depth", "dV_depth")):
         e = float(np.abs(t.grad.double().cpu().numpy() - g[k]).max()) / max(1.0, float(np.abs(g[k]).max()))
         assert e <= 3e-2, (k, e)
+
+
+# 16-bit on the tiled CUDA-core kernel: head dims the tensor-core kernel does not take,
+# and head_dim 64 / 128 with the CUDA-core kernel forced
+HALF_TILED = [(1, 4, 2, 130, 8, 3, "auto"), (2, 6, 3, 77, 36, 5, "auto"), (1, 4, 2, 200, 96, 33, "auto"),
+              (1, 8, 2, 129, 64, 4, "simt"), (1, 4, 4, 64, 128, 2, "simt")]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "f16"])
+@pytest.mark.parametrize("case", HALF_TILED, ids=[str(c) for c in HALF_TILED])
+def test_half_inputs_on_the_tiled_cuda_core_kernel(case, dtype):
+    B, Hq, Hk, T, d, L, kernel = case
+    arrs = seeded_inputs(B, Hq, Hk, T, d, L, seed=T + d)
+    args = dev(arrs, dtype)
+    if kernel == "auto":
+        assert moda_plan(*args, L) == "simt"
+    ref = orc.moda_attention_naive(*rounded(arrs, dtype), L)
+    assert max_abs(run(args, L, kernel=kernel), ref) <= BF16_ABS_TOL
