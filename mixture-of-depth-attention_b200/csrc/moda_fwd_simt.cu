@@ -1,11 +1,13 @@
-// CUDA-core MoDA forward: any dtype (f32 / bf16 / f16), any strides, d <= 256.
+// CUDA-core MoDA forward: any dtype (f32 / bf16 / f16), fp32 FMA throughout.
 //
-// This is the exact-arithmetic path (fp32 FMA throughout) used for fp32 inputs,
-// whose tolerance (1e-4 relative) tensor-core bf16/tf32 products cannot meet,
-// and for shapes the tcgen05 kernel does not tile (d not in {64,128}, G not
-// dividing 128, unaligned strides).
+// This is the path for fp32 inputs, whose tolerance (1e-4 relative) tensor-core
+// bf16/tf32 products cannot meet, and for the shapes the tcgen05 kernel does not tile
+// (16-bit head_dim outside {64, 128}, more than 128 query heads per KV head, layouts
+// TMA cannot describe). Two kernels: a tiled one (below) for d a multiple of 4 up to
+// 128 with 16-byte aligned rows, and a warp-per-row one for everything else (any
+// strides, d <= 256).
 //
-// One warp owns one query row (b, h, t). Lanes split the head dimension; every
+// Warp-per-row kernel: one warp owns one query row (b, h, t). Lanes split the head dimension; every
 // key is one warp-wide dot product, folded into a single online softmax that
 // runs over the causal keys 0..t and then over the L depth rows t*L..t*L+L-1
 // of the same KV head -- the combined softmax of moda_attention_naive
