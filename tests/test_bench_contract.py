@@ -82,3 +82,21 @@ def test_row_checker_accepts_the_oracle_and_rejects_a_planted_error():
     bad[b, h, t, 0] += 0.05
     ok, worst = bench.check_rows(bad, *ts, L, rows)
     assert not ok and abs(worst - 0.05) < 1e-6
+
+
+def test_side_pass_shape_options():
+    """--batch / --seq / --heads / --head-dim reshape the workload of the backward and
+    reference passes only, keeping its seeds; the forward headline refuses them."""
+    sys.path.insert(0, REPO)
+    import bench
+    wl = bench.WORKLOADS["kernel"]
+    r = bench.resized(wl, 1, 4096)
+    assert (r["B"], r["T"], r["Hq"], r["Hk"], r["d"], r["seed"]) == (1, 4096, 32, 8, 128, wl["seed"])
+    assert "B=1 " in r["desc"] and "T=4096 " in r["desc"]
+    assert bench.resized(wl) is wl
+    assert abs(bench.fma_peak_tflops(1965) - 74.45) < 0.01
+    for args in (["--pass", "forward", "--heads", "24,8"], ["--pass", "forward", "--dtype", "fp32"],
+                 ["--pass", "backward", "--heads", "24,7"], ["--pass", "model", "--head-dim", "96"]):
+        res = subprocess.run([sys.executable, "bench.py", *args, "--steps", "1"], cwd=REPO,
+                             capture_output=True, text=True, timeout=300)
+        assert res.returncode == 2 and "error:" in res.stderr, (args, res.stderr[-300:])
